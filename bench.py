@@ -1,0 +1,387 @@
+"""Benchmark of the fused attention forward (and the bf16 GEMM) on B200.
+
+Default workload (N=1): BASELINE config 2 -- B=4, H=32, N=4096, head_dim=128,
+non-causal, bf16 Q/K/V ~ N(0,1) from a seeded counter-based generator.  With
+--gpus N under torchrun every rank runs the same per-GPU workload on its own
+slice of a batch of 4N (sharded by batch: weak scaling, no collective on the
+data path); the box value is total FLOPs / max-over-ranks time.
+
+One JSON line on rank 0 (see the project's benchmark contract):
+  value      device-resident throughput (TFLOP/s, whole box)
+  e2e        same metric through the C-ABI call with pinned host buffers:
+             H2D of Q/K/V + kernel + D2H of O inside the timed region
+  roofline   dominant kernel vs the measured bf16 tensor peak
+  cpu_baseline  the reference's CPU attention (oracle/_ref) on a bounded
+             sample, on this host's cores (rank 0, N=1 only)
+
+--impl reference runs the reference's CPU implementation of the path (the
+compiled reference code in oracle/_ref, else the oracle restatement) on all
+host threads, each step a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "attention fwd TFLOPS per GPU and per box at 1/2/4/8 B200; % of bf16 tensor peak"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# Per-GPU workloads.  "b" is the per-GPU batch.
+WORKLOADS = {
+    "c2": dict(name="attn_b4_h32_n4096_d128", b=4, h=32, n=4096, d=128, causal=False,
+               sigma=1.0),
+    "c1": dict(name="attn_b1_h8_n1024_d128", b=1, h=8, n=1024, d=128, causal=False, sigma=1.0),
+    # config 3: H=64 sharded by head over N GPUs; per GPU shard of 8 heads at N=8.
+    "c3": dict(name="attn_b1_h64_n16384_d128_causal_per_gpu_h8", b=1, h=8, n=16384, d=128,
+               causal=True, sigma=1.0),
+    # config 4: B=64 sharded by batch over 8 GPUs: 8 per GPU.
+    "c4": dict(name="attn_b64_h16_n2048_d64_per_gpu_b8", b=8, h=16, n=2048, d=64, causal=False,
+               sigma=0.5),
+}
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel,
+# from the ncu capture summarised in profiles/ (None until captured).
+NCU_TRAFFIC_BYTES = {"c2": None}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def attention_flops(w: dict) -> float:
+    f = 4.0 * w["b"] * w["h"] * w["n"] * w["n"] * w["d"]
+    return f / 2 if w["causal"] else f
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML, sampled in a background thread)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    def __init__(self, device_index: int, period_s: float = 0.02):
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period_s
+        self._ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._ok = True
+        except Exception:
+            self._ok = False
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    _REASONS = [("hw_slowdown", "nvmlClocksThrottleReasonHwSlowdown"),
+                ("hw_thermal_slowdown", "nvmlClocksThrottleReasonHwThermalSlowdown"),
+                ("sw_thermal_slowdown", "nvmlClocksThrottleReasonSwThermalSlowdown"),
+                ("sw_power_cap", "nvmlClocksThrottleReasonSwPowerCap")]
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h,
+                                                                     self._nv.NVML_CLOCK_SM))
+                mask = self._nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                for name, attr in self._REASONS:
+                    bit = getattr(self._nv, attr, 0)
+                    if bit and (mask & bit):
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self._period)
+
+    def __enter__(self):
+        if self._ok:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._ok:
+            self._t.join()
+
+    def summary(self) -> dict:
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the reference's own CPU attention on a bounded sample
+# ---------------------------------------------------------------------------
+def _cpu_sample_inputs(w: dict, rows: int, seed: int = 1234):
+    import oracle
+    rng = np.random.default_rng(seed)
+    n, d = w["n"], w["d"]
+    q = oracle.f32_to_bf16(rng.standard_normal((1, 1, rows, d), dtype=np.float32) * w["sigma"])
+    k = oracle.f32_to_bf16(rng.standard_normal((1, 1, n, d), dtype=np.float32) * w["sigma"])
+    v = oracle.f32_to_bf16(rng.standard_normal((1, 1, n, d), dtype=np.float32) * w["sigma"])
+    return q, k, v
+
+
+def cpu_reference_sample(w: dict, rows_per_thread: int, threads: int) -> dict:
+    """Run `threads` concurrent calls of the reference CPU attention, each on
+    `rows_per_thread` query rows (the last rows of a head, so causal rows see
+    their full key range) against one full head of K/V.  Returns the wall time
+    and the FLOPs counted the harness way (4*rows*keys*d, halved for causal)."""
+    import oracle
+    use_ref = oracle.ref_available()
+    n, d = w["n"], w["d"]
+    q, k, v = _cpu_sample_inputs(w, rows_per_thread)
+    # Non-causal: rows x all keys.  Causal: the sampled rows are the LAST rows
+    # of the sequence (Sq = rows, Skv = n, bottom-right aligned) -- counted as
+    # rows * n * d * 4 / 2 like the harness counts a causal head.
+    if use_ref:
+        fn = oracle.ref().ref_attention_f32
+    else:
+        fn = None
+
+    def one(_):
+        out = np.zeros((1, 1, rows_per_thread, d), dtype=np.float32)
+        if fn is not None:
+            import ctypes
+            u16 = ctypes.POINTER(ctypes.c_uint16)
+            fn(q.ctypes.data_as(u16), k.ctypes.data_as(u16), v.ctypes.data_as(u16), 1, 1, 1,
+               rows_per_thread, n, d, float(np.float32(1.0) / np.sqrt(np.float32(d))),
+               int(w["causal"]), out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+        else:
+            out[:] = oracle.attention(q, k, v, causal=w["causal"], threads=1)
+        return out
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(one, range(threads)))
+    dt = time.perf_counter() - t0
+    flops = 4.0 * rows_per_thread * n * d * threads
+    if w["causal"]:
+        flops /= 2
+    return {"seconds": dt, "flops": flops, "kind": "reference" if use_ref else "port"}
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference_arm(args, w: dict) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = host_threads()
+    rows = args.cpu_rows
+    for _ in range(args.warmup):
+        cpu_reference_sample(w, max(1, rows // 8), threads)
+    times, flops, kind = [], 0.0, "port"
+    for _ in range(args.steps):
+        r = cpu_reference_sample(w, rows, threads)
+        times.append(r["seconds"])
+        flops, kind = r["flops"], r["kind"]
+    t = sum(times) / len(times)
+    value = flops / t / 1e12
+    sample = (f"{threads} threads x {rows} query rows x {w['n']} keys x d{w['d']}"
+              f"{' causal' if w['causal'] else ''} per step (1 head of K/V each)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,sigma) bf16 inputs",
+        "config": {"workload": w["name"], "B": w["b"], "H": w["h"], "N": w["n"], "D": w["d"],
+                   "causal": w["causal"], "sampled": True},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_gpu_arm(args, w: dict) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from benchmark_b200 import _lib, ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    B, H, N, D = w["b"], w["h"], w["n"], w["d"]
+    q = torch.empty((B, H, N, D), dtype=torch.bfloat16, device=dev)
+    k = torch.empty_like(q)
+    v = torch.empty_like(q)
+    o = torch.empty_like(q)
+    per = q.numel()
+    # this rank's batch slice of the global [B * world, H, N, D] tensors
+    for t, tid in ((q, 0), (k, 1), (v, 2)):
+        ops.fill_normal_(t, args.seed, tid, 0.0, w["sigma"], index_base=rank * per)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+
+    def step():
+        ops.attention_fwd(q, k, v, out=o, causal=w["causal"], stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    ops.check(stream)
+    barrier()
+    torch.cuda.synchronize()
+
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ops.check(stream)
+    ms = start.elapsed_time(stop) / args.steps
+    t_local = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
+    ms_max = float(t_local.item())
+    flops = attention_flops(w)
+    value = world * flops / (ms_max * 1e-3) / 1e12
+
+    # ---- e2e: pinned host in/out through the C-ABI call ----
+    hq = torch.empty(q.shape, dtype=torch.bfloat16, pin_memory=True)
+    hk = torch.empty_like(hq, pin_memory=True)
+    hv = torch.empty_like(hq, pin_memory=True)
+    ho = torch.empty_like(hq, pin_memory=True)
+    hq.copy_(q)
+    hk.copy_(k)
+    hv.copy_(v)
+    dq, dk, dv, do = (torch.empty_like(q) for _ in range(4))
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        ops.attention_fwd(dq, dk, dv, out=do, causal=w["causal"], stream=stream)
+        ho.copy_(do, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    s2 = torch.cuda.Event(enable_timing=True)
+    e2 = torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2.record(stream)
+    torch.cuda.synchronize()
+    ops.check(stream)
+    e2e_ms = torch.tensor([s2.elapsed_time(e2) / e2e_steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = world * flops / (float(e2e_ms.item()) * 1e-3) / 1e12
+    assert torch.equal(do, o), "e2e output differs from the device-resident run"
+
+    peaks, peak_src = load_peaks()
+    peak = float(peaks["bf16_tflops"])
+    achieved = flops / (ms * 1e-3) / 1e12
+    traffic = NCU_TRAFFIC_BYTES.get(args.workload)
+    algo_bytes = 4 * q.numel() * 2  # Q, K, V read + O written once
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
+        r = cpu_reference_sample(w, args.cpu_rows, threads)
+        cpu = {"value": r["flops"] / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": threads,
+               "kind": r["kind"],
+               "sample": (f"{threads} threads x {args.cpu_rows} query rows x {N} keys x d{D} "
+                          f"({r['seconds']:.1f} s wall)")}
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": f"synthetic: bf16 Q/K/V ~ N(0,{w['sigma']}^2), counter-based seed {args.seed}",
+        "config": {"workload": w["name"], "B_per_gpu": B, "global_B": B * world, "H": H,
+                   "N": N, "D": D, "causal": w["causal"],
+                   "parallelism": f"dp{world} (batch-sharded heads, no collective)",
+                   "l2": f"inputs larger than L2 ({3 * q.numel() * 2 / 2**20:.0f} MiB read per step)"},
+        "per_gpu_tflops": value / world,
+        "frac_of_peak": {"value": achieved / peak, "peak_tflops": peak, "peak_source": peak_src},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "algorithmic_bytes": algo_bytes,
+                     "kernel": f"attention_fwd_kernel<{D}>",
+                     "peak_source": f"{peak_src} bf16_tflops (burst)"},
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 3 * q.numel() * 2, "d2h_bytes_per_step": o.numel() * 2,
+                "steps": e2e_steps},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+        "lib": _lib.LIB_PATH.name,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    ap.add_argument("--seed", type=int, default=2024)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-rows", type=int, default=256,
+                    help="query rows per host thread in the CPU sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference_arm(args, w)
+    else:
+        run_gpu_arm(args, w)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,278 @@
+// C-ABI entry points (include/b200attn.h).  Single translation unit: the
+// kernels are header-only so the device status word is one symbol.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "b200attn.h"
+#include "ptx.cuh"
+#include "attention_kernel.cuh"
+#include "reference_kernels.cuh"
+
+namespace {
+
+thread_local std::string t_last_error;
+
+b200_status fail(b200_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return s;
+}
+
+b200_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(B200_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda) ----
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 3-D bf16 tensor [d2][d1][d0] (d0 contiguous), 128-byte swizzled boxes of
+// box0 x box1 x 1 elements.
+b200_status encode_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                           uint64_t d2, uint32_t box0, uint32_t box1) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(B200_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+  const cuuint32_t box[3] = {box0, box1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B200_ECUDA, "cuTensorMapEncodeTiled failed (%d) for dims %llu x %llu x %llu",
+                static_cast<int>(r), static_cast<unsigned long long>(d0),
+                static_cast<unsigned long long>(d1), static_cast<unsigned long long>(d2));
+  return B200_OK;
+}
+
+// cudaFuncSetAttribute once per (kernel, device).
+template <typename Kernel>
+b200_status ensure_smem_attr(Kernel kernel, int bytes, unsigned* done_mask) {
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(mu);
+  const unsigned bit = 1u << (dev & 31);
+  if (*done_mask & bit) return B200_OK;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+  *done_mask |= bit;
+  return B200_OK;
+}
+
+struct AttnShape {
+  int B, Hq, Hkv, Sq, Skv, D, causal;
+  float scale;
+};
+
+b200_status check_attention_args(const void* q, const void* k, const void* v, const void* o,
+                                  int B, int Hq, int Hkv, int Sq, int Skv, int D, int causal,
+                                  float softmax_scale, AttnShape* out) {
+  if (!q || !k || !v || !o) return fail(B200_EINVAL, "attention: null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(B200_EINVAL, "attention: tensor pointers must be 16-byte aligned");
+  if (B < 1 || Hq < 1 || Hkv < 1 || Sq < 1 || Skv < 1)
+    return fail(B200_EINVAL, "attention: invalid shape B=%d Hq=%d Hkv=%d Sq=%d Skv=%d", B, Hq,
+                Hkv, Sq, Skv);
+  if (Hq % Hkv != 0)
+    return fail(B200_EINVAL, "attention: requires Hq %% Hkv == 0; got Hq=%d Hkv=%d", Hq, Hkv);
+  if (D != 64 && D != 128)
+    return fail(B200_EUNSUPPORTED, "attention: head_dim must be 64 or 128; got D=%d", D);
+  const float scale = softmax_scale < 0.0f ? 1.0f / std::sqrt(static_cast<float>(D))
+                                           : softmax_scale;
+  if (!std::isfinite(scale)) return fail(B200_EINVAL, "attention: softmax_scale is not finite");
+  const long long planes_q = static_cast<long long>(B) * Hq;
+  const long long planes_kv = static_cast<long long>(B) * Hkv;
+  if (planes_q > (1ll << 31) || planes_kv > (1ll << 31))
+    return fail(B200_EUNSUPPORTED, "attention: B*H too large");
+  *out = AttnShape{B, Hq, Hkv, Sq, Skv, D, causal ? 1 : 0, scale};
+  return B200_OK;
+}
+
+template <int D>
+b200_status launch_attention(const void* q, const void* k, const void* v, void* o,
+                             const AttnShape& s, cudaStream_t stream) {
+  using C = b200::attn::Cfg<D>;
+  static unsigned attr_done = 0;
+  auto kernel = b200::attn::attention_fwd_kernel<D>;
+  b200_status st = ensure_smem_attr(kernel, C::kSmemBytes, &attr_done);
+  if (st != B200_OK) return st;
+
+  CUtensorMap qm, km, vm, om;
+  const uint64_t pq = static_cast<uint64_t>(s.B) * s.Hq;
+  const uint64_t pkv = static_cast<uint64_t>(s.B) * s.Hkv;
+  if ((st = encode_bf16_3d(&qm, q, D, s.Sq, pq, 64, 128)) != B200_OK) return st;
+  if ((st = encode_bf16_3d(&km, k, D, s.Skv, pkv, 64, 128)) != B200_OK) return st;
+  if ((st = encode_bf16_3d(&vm, v, D, s.Skv, pkv, 64, 128)) != B200_OK) return st;
+  if ((st = encode_bf16_3d(&om, o, D, s.Sq, pq, 64, 128)) != B200_OK) return st;
+
+  b200::attn::Params p{};
+  p.B = s.B;
+  p.Hq = s.Hq;
+  p.Hkv = s.Hkv;
+  p.Sq = s.Sq;
+  p.Skv = s.Skv;
+  p.group = s.Hq / s.Hkv;
+  p.n_qpairs = (s.Sq + 2 * b200::attn::kBM - 1) / (2 * b200::attn::kBM);
+  p.causal = s.causal;
+  p.causal_off = s.Skv - s.Sq;
+  p.scale_log2 = s.scale * 1.4426950408889634f;
+  const long long grid = static_cast<long long>(pq) * p.n_qpairs;
+  if (grid > 0x7fffffffll) return fail(B200_EUNSUPPORTED, "attention: grid too large");
+  kernel<<<static_cast<unsigned>(grid), b200::attn::kThreads, C::kSmemBytes, stream>>>(qm, km,
+                                                                                      vm, om, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attention_fwd launch");
+  return B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* b200_last_error(void) { return t_last_error.c_str(); }
+
+int b200_version(void) { return 100; }
+
+b200_status attention_fwd(const void* q, const void* k, const void* v, void* o, int B, int Hq,
+                          int Hkv, int Sq, int Skv, int D, int causal, float softmax_scale,
+                          b200_stream_t stream) {
+  AttnShape s;
+  b200_status st = check_attention_args(q, k, v, o, B, Hq, Hkv, Sq, Skv, D, causal,
+                                        softmax_scale, &s);
+  if (st != B200_OK) return st;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  return D == 128 ? launch_attention<128>(q, k, v, o, s, cs)
+                  : launch_attention<64>(q, k, v, o, s, cs);
+}
+
+b200_status attention_fwd_scalar(const void* q, const void* k, const void* v, void* o, int B,
+                                 int Hq, int Hkv, int Sq, int Skv, int D, int causal,
+                                 float softmax_scale, b200_stream_t stream) {
+  AttnShape s;
+  b200_status st = check_attention_args(q, k, v, o, B, Hq, Hkv, Sq, Skv, D, causal,
+                                        softmax_scale, &s);
+  if (st != B200_OK) return st;
+  if (static_cast<long long>(B) * Hq > 65535)
+    return fail(B200_EUNSUPPORTED, "attention_fwd_scalar: B*Hq must be <= 65535");
+  b200::ref::ScalarParams p{};
+  p.q = static_cast<const uint16_t*>(q);
+  p.k = static_cast<const uint16_t*>(k);
+  p.v = static_cast<const uint16_t*>(v);
+  p.o = static_cast<uint16_t*>(o);
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.Sq = Sq;
+  p.Skv = Skv;
+  p.group = Hq / Hkv;
+  p.causal = s.causal;
+  p.scale = s.scale;
+  const dim3 grid((Sq + 3) / 4, B * Hq);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  if (D == 128)
+    b200::ref::attention_scalar_kernel<128><<<grid, 128, 0, cs>>>(p);
+  else
+    b200::ref::attention_scalar_kernel<64><<<grid, 128, 0, cs>>>(p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attention_fwd_scalar launch");
+  return B200_OK;
+}
+
+b200_status b200_fill_normal_bf16(void* dst, uint64_t n, uint64_t seed, uint32_t tensor_id,
+                                  uint64_t index_base, float mean, float sigma,
+                                  b200_stream_t stream) {
+  if (n == 0) return B200_OK;
+  if (!dst) return fail(B200_EINVAL, "fill: null pointer");
+  const uint64_t key = b200::ref::stream_key(seed, tensor_id);
+  const unsigned blocks = static_cast<unsigned>(std::min<uint64_t>((n + 255) / 256, 148 * 32));
+  b200::ref::fill_normal_bf16_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint16_t*>(dst), n, key, index_base, mean, sigma);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fill_normal launch");
+  return B200_OK;
+}
+
+b200_status b200_fill_uniform_bf16(void* dst, uint64_t n, uint64_t seed, uint32_t tensor_id,
+                                   uint64_t index_base, float lo, float hi,
+                                   b200_stream_t stream) {
+  if (n == 0) return B200_OK;
+  if (!dst) return fail(B200_EINVAL, "fill: null pointer");
+  const uint64_t key = b200::ref::stream_key(seed, tensor_id);
+  const unsigned blocks = static_cast<unsigned>(std::min<uint64_t>((n + 255) / 256, 148 * 32));
+  b200::ref::fill_uniform_bf16_kernel<<<blocks, 256, 0,
+                                        reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint16_t*>(dst), n, key, index_base, lo, hi);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fill_uniform launch");
+  return B200_OK;
+}
+
+b200_status b200_check(b200_stream_t stream) {
+  cudaError_t e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  uint32_t status = 0;
+  e = cudaMemcpyFromSymbol(&status, b200::g_status, sizeof(status));
+  if (e != cudaSuccess) return cuda_fail(e, "read status word");
+  if (status != 0) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(b200::g_status, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_fail(e, "clear status word");
+    return fail(B200_ETIMEOUT, "device wait timed out (status 0x%08x, site %u)", status,
+                (status >> 8) & 0xffu);
+  }
+  return B200_OK;
+}
+
+}  // extern "C"
+
+namespace {
+__global__ void selftest_wait_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  b200::mbar_init(&bar, 1);
+  b200::fence_mbar_init();
+  // Nothing ever arrives: the bounded wait must give up and report.
+  (void)b200::mbar_wait(&bar, 0, 0xEE, limit_ns);
+}
+}  // namespace
+
+extern "C" b200_status b200_selftest_wait_timeout(uint64_t limit_ns, b200_stream_t stream) {
+  if (limit_ns < 1000) limit_ns = 1000;
+  if (limit_ns > 100000000ull) limit_ns = 100000000ull;
+  selftest_wait_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(limit_ns);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "selftest launch");
+  return B200_OK;
+}

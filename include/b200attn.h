@@ -1,0 +1,105 @@
+/*
+ * b200attn -- C ABI of the sm_100a fused attention forward and bf16 GEMM.
+ *
+ * The reference (rhrnald/benchmark) has no library boundary: its harness
+ * launches kernels directly.  Each entry point below replaces one such launch
+ * site; the citation after it names the reference code it stands in for
+ * (paths relative to the reference project root).
+ *
+ * Conventions
+ *   - All tensor pointers are device pointers owned by the caller, 16-byte
+ *     aligned, contiguous.  Nothing here allocates on the hot path.
+ *   - bf16 tensors are passed as raw 16-bit words (uint16_t storage).
+ *   - Calls are asynchronous on `stream` (NULL = legacy default stream) and
+ *     use the calling thread's current CUDA device.
+ *   - Errors are returned as b200_status, never by exit(); a message for the
+ *     most recent failure on the calling thread is in b200_last_error().
+ *   - Device-side waits are bounded.  A kernel whose pipeline wait runs out
+ *     records it in a per-device status word; b200_check() synchronises the
+ *     stream, reports B200_ETIMEOUT and clears the word.  While the word is
+ *     set, later kernels on that device abandon their work early.
+ */
+#ifndef B200ATTN_H
+#define B200ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; spelled out so C callers need no CUDA headers. */
+typedef struct CUstream_st* b200_stream_t;
+
+typedef enum {
+  B200_OK = 0,
+  B200_EINVAL = 1,       /* bad argument: null/misaligned pointer, bad shape */
+  B200_EUNSUPPORTED = 2, /* valid request this build does not implement */
+  B200_ECUDA = 3,        /* CUDA runtime / driver error */
+  B200_ETIMEOUT = 4      /* a device-side bounded wait ran out */
+} b200_status;
+
+/*
+ * Fused attention forward: O = softmax(Q K^T * scale) V, bf16 in / bf16 out,
+ * fp32 accumulation and softmax.
+ *   q, o : [B, Hq,  Sq,  D]      k, v : [B, Hkv, Skv, D]
+ *   D in {64, 128}; Hq % Hkv == 0 (query head h reads kv head h / (Hq/Hkv));
+ *   causal != 0: key j is visible to query i iff j <= i + (Skv - Sq)
+ *   (bottom-right aligned); rows with no visible key produce zeros.
+ *   softmax_scale < 0 selects 1/sqrt(D).
+ * Replaces the launch of qk_tma_mma_ld_kernel in 0.attention/main.cu:521-569
+ * (benchmark) and 0.attention/main.cu:1901-1911 (fused validation); accepts
+ * every shape the scalar path accepts (0.attention/main.cu:1706-1721) plus D=64.
+ */
+b200_status attention_fwd(const void* q, const void* k, const void* v, void* o, int B, int Hq,
+                          int Hkv, int Sq, int Skv, int D, int causal, float softmax_scale,
+                          b200_stream_t stream);
+
+/*
+ * Validation-only CUDA-core attention with the same arguments and semantics
+ * (exact two-pass softmax with expf, fp32).  Replaces the launch of
+ * real_attention_bf16_d128_kernel in 0.attention/main.cu:1776-1779; also
+ * accepts D=64.  Requires B*Hq <= 65535.
+ */
+b200_status attention_fwd_scalar(const void* q, const void* k, const void* v, void* o, int B,
+                                 int Hq, int Hkv, int Sq, int Skv, int D, int causal,
+                                 float softmax_scale, b200_stream_t stream);
+
+/*
+ * Seeded bf16 generators (counter-based: value = f(seed, tensor_id,
+ * index_base + i)), so any shard of a tensor can be generated independently.
+ * Stand in for the benchmark fill fill_packed_bf16 (0.attention/attention.cu:142-147,
+ * launched at 0.attention/main.cu:2068-2075), which has no seed or distribution.
+ */
+b200_status b200_fill_normal_bf16(void* dst, uint64_t n, uint64_t seed, uint32_t tensor_id,
+                                  uint64_t index_base, float mean, float sigma,
+                                  b200_stream_t stream);
+b200_status b200_fill_uniform_bf16(void* dst, uint64_t n, uint64_t seed, uint32_t tensor_id,
+                                   uint64_t index_base, float lo, float hi,
+                                   b200_stream_t stream);
+
+/* Synchronise `stream`, then read and clear the device status word.
+ * Stands in for the RunResult.status checks of 0.attention/main.cu:541-592. */
+b200_status b200_check(b200_stream_t stream);
+
+/* Message for the most recent failure on this thread ("" if none). */
+const char* b200_last_error(void);
+
+/* ABI version: major * 10000 + minor * 100 + patch. */
+int b200_version(void);
+
+/*
+ * Self-test of the bounded-wait machinery: launches one thread that waits on
+ * an mbarrier nothing ever arrives at, with the given limit (clamped to
+ * [1 us, 100 ms]).  After b200_check() the caller must see B200_ETIMEOUT.
+ * No reference counterpart (the reference's waits are unbounded,
+ * 0.attention/ptx_wrappers.cuh:195-211).
+ */
+b200_status b200_selftest_wait_timeout(uint64_t limit_ns, b200_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200ATTN_H */
