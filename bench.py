@@ -72,7 +72,7 @@ def attention_flops(w: dict) -> float:
 # clocks during the timed region (NVML, sampled in a background thread)
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    def __init__(self, device_index: int, period_s: float = 0.02):
+    def __init__(self, device_index: int, period_s: float = 0.005):
         self.samples: list[int] = []
         self.reasons: set[str] = set()
         self.max_mhz = None
@@ -118,6 +118,16 @@ class ClockSampler:
         self._stop.set()
         if self._ok:
             self._t.join()
+            self._stop.clear()
+            self._period = 0.0
+            self._stop.set()
+            self._run_once()
+
+    def _run_once(self):
+        try:
+            self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+        except Exception:
+            pass
 
     def summary(self) -> dict:
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
@@ -218,6 +228,49 @@ def run_reference_arm(args, w: dict) -> None:
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+def run_e2e(args, w, q, k, v, o, stream, world, dev, barrier, flops) -> dict:
+    """Same metric through the C-ABI call with host buffers: every step copies
+    Q/K/V from pinned host memory, runs the kernel and copies O back."""
+    import torch
+    import torch.distributed as dist
+
+    from benchmark_b200 import ops
+
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    ho = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
+    dq, dk, dv, do = (torch.empty_like(q) for _ in range(4))
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        ops.attention_fwd(dq, dk, dv, out=do, causal=w["causal"], stream=stream)
+        ho.copy_(do, non_blocking=True)
+
+    steps = max(1, min(args.steps, args.e2e_steps))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    e.record(stream)
+    torch.cuda.synchronize()
+    ops.check(stream)
+    ms = torch.tensor([s.elapsed_time(e) / steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    if not torch.equal(ho, o.cpu()):
+        raise RuntimeError("e2e output differs from the device-resident run")
+    return {"value": world * flops / (float(ms.item()) * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
+            "d2h_bytes_per_step": o.numel() * o.element_size(), "steps": steps,
+            "ms_per_step": float(ms.item())}
+
+
 def run_gpu_arm(args, w: dict) -> None:
     import torch
     import torch.distributed as dist
@@ -278,47 +331,14 @@ def run_gpu_arm(args, w: dict) -> None:
     flops = attention_flops(w)
     value = world * flops / (ms_max * 1e-3) / 1e12
 
-    # ---- e2e: pinned host in/out through the C-ABI call ----
-    hq = torch.empty(q.shape, dtype=torch.bfloat16, pin_memory=True)
-    hk = torch.empty_like(hq, pin_memory=True)
-    hv = torch.empty_like(hq, pin_memory=True)
-    ho = torch.empty_like(hq, pin_memory=True)
-    hq.copy_(q)
-    hk.copy_(k)
-    hv.copy_(v)
-    dq, dk, dv, do = (torch.empty_like(q) for _ in range(4))
-
-    def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        ops.attention_fwd(dq, dk, dv, out=do, causal=w["causal"], stream=stream)
-        ho.copy_(do, non_blocking=True)
-
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier()
-    s2 = torch.cuda.Event(enable_timing=True)
-    e2 = torch.cuda.Event(enable_timing=True)
-    s2.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e2.record(stream)
-    torch.cuda.synchronize()
-    ops.check(stream)
-    e2e_ms = torch.tensor([s2.elapsed_time(e2) / e2e_steps], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = world * flops / (float(e2e_ms.item()) * 1e-3) / 1e12
-    assert torch.equal(do, o), "e2e output differs from the device-resident run"
+    e2e = None if args.no_e2e else run_e2e(args, w, q, k, v, o, stream, world, dev, barrier,
+                                           flops)
 
     peaks, peak_src = load_peaks()
     peak = float(peaks["bf16_tflops"])
     achieved = flops / (ms * 1e-3) / 1e12
     traffic = NCU_TRAFFIC_BYTES.get(args.workload)
-    algo_bytes = 4 * q.numel() * 2  # Q, K, V read + O written once
+    algo_bytes = 4 * q.numel() * q.element_size()  # Q, K, V read + O written once
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -342,17 +362,15 @@ def run_gpu_arm(args, w: dict) -> None:
         "config": {"workload": w["name"], "B_per_gpu": B, "global_B": B * world, "H": H,
                    "N": N, "D": D, "causal": w["causal"],
                    "parallelism": f"dp{world} (batch-sharded heads, no collective)",
-                   "l2": f"inputs larger than L2 ({3 * q.numel() * 2 / 2**20:.0f} MiB read per step)"},
+                   "l2": (f"inputs larger than L2 ({3 * q.numel() * 2 / 2**20:.0f} MiB of "
+                          "Q/K/V read per step)")},
         "per_gpu_tflops": value / world,
-        "frac_of_peak": {"value": achieved / peak, "peak_tflops": peak, "peak_source": peak_src},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "algorithmic_bytes": algo_bytes,
                      "kernel": f"attention_fwd_kernel<{D}>",
                      "peak_source": f"{peak_src} bf16_tflops (burst)"},
-        "e2e": {"value": e2e_value, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": 3 * q.numel() * 2, "d2h_bytes_per_step": o.numel() * 2,
-                "steps": e2e_steps},
+        "e2e": e2e,
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
@@ -373,6 +391,7 @@ def main() -> None:
     ap.add_argument("--cpu-rows", type=int, default=256,
                     help="query rows per host thread in the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
