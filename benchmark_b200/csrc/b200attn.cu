@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -121,22 +122,44 @@ b200_status check_attention_args(const void* q, const void* k, const void* v, co
   return B200_OK;
 }
 
-template <int D>
+// FMA-pipe exp2 share (pairs of every 8) per head_dim; B200_ATTN_EXP2_EMU
+// overrides it for tuning sweeps (values without an instantiation are rejected).
+constexpr int kDefaultEmuD128 = 0;
+constexpr int kDefaultEmuD64 = 0;
+
+int exp2_emu_setting(int D) {
+  static const int env_value = [] {
+    const char* e = std::getenv("B200_ATTN_EXP2_EMU");
+    return e ? std::atoi(e) : -1;
+  }();
+  if (env_value >= 0) return env_value;
+  return D == 128 ? kDefaultEmuD128 : kDefaultEmuD64;
+}
+
+struct TraceArgs {
+  unsigned long long* buf = nullptr;
+  int cap = 0;
+  int cta = -1;
+};
+
+template <int D, int EMU, bool TRACE = false>
 b200_status launch_attention(const void* q, const void* k, const void* v, void* o,
-                             const AttnShape& s, cudaStream_t stream) {
+                             const AttnShape& s, cudaStream_t stream,
+                             const TraceArgs& tr = TraceArgs{}) {
   using C = b200::attn::Cfg<D>;
   static unsigned attr_done = 0;
-  auto kernel = b200::attn::attention_fwd_kernel<D>;
+  auto kernel = b200::attn::attention_fwd_kernel<D, EMU, TRACE>;
   b200_status st = ensure_smem_attr(kernel, C::kSmemBytes, &attr_done);
   if (st != B200_OK) return st;
 
   CUtensorMap qm, km, vm, om;
   const uint64_t pq = static_cast<uint64_t>(s.B) * s.Hq;
   const uint64_t pkv = static_cast<uint64_t>(s.B) * s.Hkv;
-  if ((st = encode_bf16_3d(&qm, q, D, s.Sq, pq, 64, 128)) != B200_OK) return st;
-  if ((st = encode_bf16_3d(&km, k, D, s.Skv, pkv, 64, 128)) != B200_OK) return st;
-  if ((st = encode_bf16_3d(&vm, v, D, s.Skv, pkv, 64, 128)) != B200_OK) return st;
-  if ((st = encode_bf16_3d(&om, o, D, s.Sq, pq, 64, 128)) != B200_OK) return st;
+  constexpr uint32_t kRows = b200::attn::kBM, kKvRows = b200::attn::kBN;
+  if ((st = encode_bf16_3d(&qm, q, D, s.Sq, pq, 64, kRows)) != B200_OK) return st;
+  if ((st = encode_bf16_3d(&km, k, D, s.Skv, pkv, 64, kKvRows)) != B200_OK) return st;
+  if ((st = encode_bf16_3d(&vm, v, D, s.Skv, pkv, 64, kKvRows)) != B200_OK) return st;
+  if ((st = encode_bf16_3d(&om, o, D, s.Sq, pq, 64, kRows)) != B200_OK) return st;
 
   b200::attn::Params p{};
   p.B = s.B;
@@ -149,6 +172,9 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   p.causal = s.causal;
   p.causal_off = s.Skv - s.Sq;
   p.scale_log2 = s.scale * 1.4426950408889634f;
+  p.trace = tr.buf;
+  p.trace_cap = tr.cap;
+  p.trace_cta = tr.cta;
   const long long grid = static_cast<long long>(pq) * p.n_qpairs;
   if (grid > 0x7fffffffll) return fail(B200_EUNSUPPORTED, "attention: grid too large");
   kernel<<<static_cast<unsigned>(grid), b200::attn::kThreads, C::kSmemBytes, stream>>>(qm, km,
@@ -156,6 +182,20 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "attention_fwd launch");
   return B200_OK;
+}
+
+template <int D>
+b200_status dispatch_attention(const void* q, const void* k, const void* v, void* o,
+                               const AttnShape& s, cudaStream_t stream) {
+  switch (exp2_emu_setting(D)) {
+    case 0: return launch_attention<D, 0>(q, k, v, o, s, stream);
+    case 1: return launch_attention<D, 1>(q, k, v, o, s, stream);
+    case 2: return launch_attention<D, 2>(q, k, v, o, s, stream);
+    case 3: return launch_attention<D, 3>(q, k, v, o, s, stream);
+    case 4: return launch_attention<D, 4>(q, k, v, o, s, stream);
+    default:
+      return fail(B200_EINVAL, "B200_ATTN_EXP2_EMU must be 0..4; got %d", exp2_emu_setting(D));
+  }
 }
 
 }  // namespace
@@ -174,8 +214,24 @@ b200_status attention_fwd(const void* q, const void* k, const void* v, void* o, 
                                         softmax_scale, &s);
   if (st != B200_OK) return st;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  return D == 128 ? launch_attention<128>(q, k, v, o, s, cs)
-                  : launch_attention<64>(q, k, v, o, s, cs);
+  return D == 128 ? dispatch_attention<128>(q, k, v, o, s, cs)
+                  : dispatch_attention<64>(q, k, v, o, s, cs);
+}
+
+b200_status attention_fwd_trace(const void* q, const void* k, const void* v, void* o, int B,
+                                int Hq, int Hkv, int Sq, int Skv, int D, int causal,
+                                float softmax_scale, unsigned long long* trace, int trace_cap,
+                                int trace_cta, b200_stream_t stream) {
+  AttnShape s;
+  b200_status st = check_attention_args(q, k, v, o, B, Hq, Hkv, Sq, Skv, D, causal,
+                                        softmax_scale, &s);
+  if (st != B200_OK) return st;
+  if (!trace || trace_cap < 1 || trace_cta < 0)
+    return fail(B200_EINVAL, "attention_fwd_trace: need a trace buffer, cap >= 1, cta >= 0");
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const TraceArgs tr{trace, trace_cap, trace_cta};
+  return D == 128 ? launch_attention<128, kDefaultEmuD128, true>(q, k, v, o, s, cs, tr)
+                  : launch_attention<64, kDefaultEmuD64, true>(q, k, v, o, s, cs, tr);
 }
 
 b200_status attention_fwd_scalar(const void* q, const void* k, const void* v, void* o, int B,

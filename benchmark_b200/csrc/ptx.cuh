@@ -61,25 +61,45 @@ __device__ __forceinline__ void fence_mbar_init() {
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
                    smem_u32(bar)),
                "r"(bytes)
                : "memory");
 }
 
+// Non-blocking check of a phase (acquire semantics at CTA scope).  A
+// test_wait whose result is branched on stalls the thread for its latency
+// (hundreds of cycles on B200), so hot waits poll several barriers at once
+// (mbar_test3) and keep their slow loop out of line.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n .reg .pred p;\n"
-      " mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+      " mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
       : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Blocking variant: the thread may sleep inside the instruction (up to
+// hint_ns) until the phase completes, so waiting warps stop competing for
+// issue slots with the warps that share their scheduler.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
@@ -89,16 +109,12 @@ __device__ __noinline__ void report_timeout(uint32_t site) {
   atomicCAS(&g_status, 0u, kStatusTimeout | ((site & 0xffu) << 8));
 }
 
-// Wait until the phase with the given parity has completed.  Returns false if
-// the limit ran out or another wait anywhere on the device already gave up;
-// callers then unwind without issuing further dependent work.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site,
-                                          uint64_t limit_ns = kDefaultWaitLimitNs) {
-  const uint32_t addr = smem_u32(bar);
-  if (mbar_try_wait(addr, parity)) return true;
+__device__ __noinline__ bool mbar_wait_slow(uint32_t addr, uint32_t parity, uint32_t site,
+                                            uint64_t limit_ns, uint32_t sleep_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(addr, parity)) return true;
+    if (sleep_ns ? mbar_try_wait_sleep(addr, parity, sleep_ns) : mbar_try_wait(addr, parity))
+      return true;
     if ((it & 31u) == 0) {
       if (*reinterpret_cast<volatile uint32_t*>(&g_status) != 0u) return false;
       if (globaltimer_ns() - t0 > limit_ns) {
@@ -107,6 +123,57 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
       }
     }
   }
+}
+
+// Wait until the phase with the given parity has completed.  Returns false if
+// the limit ran out or another wait anywhere on the device already gave up;
+// callers then unwind without issuing further dependent work.  sleep_ns > 0
+// lets the thread sleep in the hardware wait between polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site,
+                                          uint64_t limit_ns = kDefaultWaitLimitNs,
+                                          uint32_t sleep_ns = 0) {
+  const uint32_t addr = smem_u32(bar);
+  return mbar_try_wait(addr, parity) || mbar_wait_slow(addr, parity, site, limit_ns, sleep_ns);
+}
+
+// Poll three barriers in one instruction group: the test_waits do not depend
+// on each other, so their latencies overlap instead of adding up.  Pass an
+// already-completed (barrier, parity) to fill unused slots.
+__device__ __forceinline__ bool mbar_test3(uint32_t a0, uint32_t p0, uint32_t a1, uint32_t p1,
+                                           uint32_t a2, uint32_t p2) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred q0, q1, q2;\n"
+      " mbarrier.test_wait.parity.shared::cta.b64 q0, [%1], %2;\n"
+      " mbarrier.test_wait.parity.shared::cta.b64 q1, [%3], %4;\n"
+      " mbarrier.test_wait.parity.shared::cta.b64 q2, [%5], %6;\n"
+      " and.pred q0, q0, q1;\n and.pred q0, q0, q2;\n"
+      " selp.u32 %0, 1, 0, q0;\n}\n"
+      : "=r"(ok)
+      : "r"(a0), "r"(p0), "r"(a1), "r"(p1), "r"(a2), "r"(p2)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __noinline__ bool mbar_wait3_slow(uint32_t a0, uint32_t p0, uint32_t a1, uint32_t p1,
+                                             uint32_t a2, uint32_t p2, uint32_t site) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_test3(a0, p0, a1, p1, a2, p2)) return true;
+    if ((it & 31u) == 0) {
+      if (*reinterpret_cast<volatile uint32_t*>(&g_status) != 0u) return false;
+      if (globaltimer_ns() - t0 > kDefaultWaitLimitNs) {
+        report_timeout(site);
+        return false;
+      }
+    }
+  }
+}
+
+// Bounded wait for three phases at once (fast path inline, loop out of line).
+__device__ __forceinline__ bool mbar_wait3(uint32_t a0, uint32_t p0, uint32_t a1, uint32_t p1,
+                                           uint32_t a2, uint32_t p2, uint32_t site) {
+  return mbar_test3(a0, p0, a1, p1, a2, p2) || mbar_wait3_slow(a0, p0, a1, p1, a2, p2, site);
 }
 
 // ---------------------------------------------------------------------------
@@ -340,6 +407,64 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): lo in bits 0-31.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// exp2 of two values on the FMA pipe, for inputs in [-126, 127):
+//   x = j + r with j = round(x) (adding 1.5 * 2^23 leaves round(x) in the low
+//   mantissa bits of t), r in [-0.5, 0.5];  2^r ~ c0 + r(c1 + r(c2 + r c3)),
+//   a degree-3 minimax fit of the relative error (7.5e-5) produced by
+//   benchmark_b200/csrc/fit_exp2_poly.py;  2^j is applied by adding j << 23
+//   to the exponent field (t's bit pattern << 23 is exactly j << 23).
+// Inputs are clamped to >= -126 so the exponent never underflows.
+__device__ __forceinline__ void exp2_fma_x2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t x = f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const uint64_t t = f2_add(x, magic);
+  const uint64_t r = f2_sub(x, f2_sub(t, magic));
+  uint64_t p = f2_fma(f2_pack(0.0551716685295105f, 0.0551716685295105f), r,
+                      f2_pack(0.2426111251115799f, 0.2426111251115799f));
+  p = f2_fma(p, r, f2_pack(0.6932609677314758f, 0.6932609677314758f));
+  p = f2_fma(p, r, f2_pack(0.9999280571937561f, 0.9999280571937561f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
 // Two fp32 -> packed bf16x2 (round to nearest even); lo in bits 0-15.

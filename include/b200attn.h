@@ -57,6 +57,21 @@ b200_status attention_fwd(const void* q, const void* k, const void* v, void* o, 
                           b200_stream_t stream);
 
 /*
+ * attention_fwd with clock-cycle tracing of one CTA (diagnostics; runs the
+ * default exp2 split).  trace: device buffer of 4 * trace_cap * 2 uint64
+ * (zero it first).  Role r (0 TMA producer, 1 MMA issuer, 2 and 3 softmax of
+ * Q tile 0 and 1) writes up to trace_cap records at trace + r*trace_cap*2,
+ * each {(event << 32) | (tile << 24) | iteration, clock64()}.  Events are
+ * listed in benchmark_b200/trace.py.  Stands in for the reference's
+ * ATTENTION_CLOCK_TRACE build and its per-stage CSV
+ * (0.attention/main.cu:175-272, 0.attention/main.cu:808-1157).
+ */
+b200_status attention_fwd_trace(const void* q, const void* k, const void* v, void* o, int B,
+                                int Hq, int Hkv, int Sq, int Skv, int D, int causal,
+                                float softmax_scale, unsigned long long* trace, int trace_cap,
+                                int trace_cta, b200_stream_t stream);
+
+/*
  * Validation-only CUDA-core attention with the same arguments and semantics
  * (exact two-pass softmax with expf, fp32).  Replaces the launch of
  * real_attention_bf16_d128_kernel in 0.attention/main.cu:1776-1779; also
