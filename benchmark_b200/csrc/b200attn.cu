@@ -15,6 +15,10 @@
 #include "ptx.cuh"
 #include "attention_kernel.cuh"
 #include "reference_kernels.cuh"
+#include "gemm_kernel.cuh"
+
+#include <cublas_v2.h>
+#include <map>
 
 namespace {
 
@@ -74,6 +78,26 @@ b200_status encode_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint
     return fail(B200_ECUDA, "cuTensorMapEncodeTiled failed (%d) for dims %llu x %llu x %llu",
                 static_cast<int>(r), static_cast<unsigned long long>(d0),
                 static_cast<unsigned long long>(d1), static_cast<unsigned long long>(d2));
+  return B200_OK;
+}
+
+// 2-D bf16 tensor [d1][d0] (d0 contiguous), 128-byte swizzled boxes.
+b200_status encode_bf16_2d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                           uint32_t box0, uint32_t box1) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(B200_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const cuuint64_t dims[2] = {d0, d1};
+  const cuuint64_t strides[1] = {d0 * 2};
+  const cuuint32_t box[2] = {box0, box1};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B200_ECUDA, "cuTensorMapEncodeTiled failed (%d) for dims %llu x %llu",
+                static_cast<int>(r), static_cast<unsigned long long>(d0),
+                static_cast<unsigned long long>(d1));
   return B200_OK;
 }
 
@@ -196,6 +220,45 @@ b200_status dispatch_attention(const void* q, const void* k, const void* v, void
     default:
       return fail(B200_EINVAL, "B200_ATTN_EXP2_EMU must be 0..4; got %d", exp2_emu_setting(D));
   }
+}
+
+b200_status check_gemm_args(const void* A, const void* Bm, const void* C, int M, int N, int K,
+                            const char* who) {
+  if (!A || !Bm || !C) return fail(B200_EINVAL, "%s: null matrix pointer", who);
+  if (!aligned16(A) || !aligned16(Bm) || !aligned16(C))
+    return fail(B200_EINVAL, "%s: matrix pointers must be 16-byte aligned", who);
+  if (M < 1 || N < 1 || K < 1)
+    return fail(B200_EINVAL, "%s: invalid shape M=%d N=%d K=%d", who, M, N, K);
+  if (K % 8 != 0 || N % 8 != 0)
+    return fail(B200_EUNSUPPORTED, "%s: K and N must be multiples of 8 (16-byte rows); got "
+                "N=%d K=%d", who, N, K);
+  return B200_OK;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return n > 0 ? n : 148;
+}
+
+// One cuBLAS handle per (thread, device) for the comparator.
+cublasHandle_t cublas_handle(b200_status* st) {
+  thread_local std::map<int, cublasHandle_t> handles;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    *st = fail(B200_ECUDA, "cudaGetDevice");
+    return nullptr;
+  }
+  auto it = handles.find(dev);
+  if (it != handles.end()) return it->second;
+  cublasHandle_t h = nullptr;
+  if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) {
+    *st = fail(B200_ECUDA, "cublasCreate failed");
+    return nullptr;
+  }
+  handles[dev] = h;
+  return h;
 }
 
 }  // namespace
@@ -330,5 +393,71 @@ extern "C" b200_status b200_selftest_wait_timeout(uint64_t limit_ns, b200_stream
   selftest_wait_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(limit_ns);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "selftest launch");
+  return B200_OK;
+}
+
+extern "C" b200_status gemm_bf16(const void* A, const void* Bm, void* C, int M, int N, int K,
+                                 int b_col_major, b200_stream_t stream) {
+  b200_status st = check_gemm_args(A, Bm, C, M, N, K, "gemm_bf16");
+  if (st != B200_OK) return st;
+  static unsigned attr_done = 0;
+  st = ensure_smem_attr(b200::gemm::gemm_bf16_kernel, b200::gemm::kSmemBytes, &attr_done);
+  if (st != B200_OK) return st;
+  CUtensorMap am, bm;
+  if ((st = encode_bf16_2d(&am, A, K, M, b200::gemm::kBK, b200::gemm::kBM)) != B200_OK) return st;
+  if (b_col_major)
+    st = encode_bf16_2d(&bm, Bm, K, N, b200::gemm::kBK, b200::gemm::kBN);
+  else
+    st = encode_bf16_2d(&bm, Bm, N, K, 64, b200::gemm::kBK);
+  if (st != B200_OK) return st;
+  b200::gemm::Params p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.tiles_m = (M + b200::gemm::kBM - 1) / b200::gemm::kBM;
+  p.tiles_n = (N + b200::gemm::kBN - 1) / b200::gemm::kBN;
+  p.k_blocks = (K + b200::gemm::kBK - 1) / b200::gemm::kBK;
+  p.b_col_major = b_col_major ? 1 : 0;
+  p.C = static_cast<uint16_t*>(C);
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  if (tiles > 0x7fffffffll) return fail(B200_EUNSUPPORTED, "gemm_bf16: too many tiles");
+  const int grid = static_cast<int>(std::min<long long>(tiles, sm_count()));
+  b200::gemm::gemm_bf16_kernel<<<grid, b200::gemm::kThreads, b200::gemm::kSmemBytes,
+                                 reinterpret_cast<cudaStream_t>(stream)>>>(am, bm, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16 launch");
+  return B200_OK;
+}
+
+extern "C" b200_status gemm_bf16_cublas(const void* A, const void* Bm, void* C, int M, int N,
+                                        int K, int b_col_major, b200_stream_t stream) {
+  b200_status st = check_gemm_args(A, Bm, C, M, N, K, "gemm_bf16_cublas");
+  if (st != B200_OK) return st;
+  cublasHandle_t h = cublas_handle(&st);
+  if (!h) return st;
+  if (cublasSetStream(h, reinterpret_cast<cudaStream_t>(stream)) != CUBLAS_STATUS_SUCCESS)
+    return fail(B200_ECUDA, "cublasSetStream failed");
+  // Row-major C = A B is column-major C^T = B^T A^T: cuBLAS sees A as a
+  // column-major K x M matrix (op N) and B as K x N column-major if it is
+  // stored [N,K] (op T), or N x K column-major if stored [K,N] (op N).
+  const float alpha = 1.0f, beta = 0.0f;
+  const cublasStatus_t r = cublasGemmEx(
+      h, b_col_major ? CUBLAS_OP_T : CUBLAS_OP_N, CUBLAS_OP_N, N, M, K, &alpha, Bm, CUDA_R_16BF,
+      b_col_major ? K : N, A, CUDA_R_16BF, K, &beta, C, CUDA_R_16BF, N, CUBLAS_COMPUTE_32F,
+      CUBLAS_GEMM_DEFAULT);
+  if (r != CUBLAS_STATUS_SUCCESS) return fail(B200_ECUDA, "cublasGemmEx failed (%d)", (int)r);
+  return B200_OK;
+}
+
+extern "C" b200_status gemm_f32_reference(const void* A, const void* Bm, void* C, int M, int N,
+                                          int K, int b_col_major, b200_stream_t stream) {
+  if (!A || !Bm || !C) return fail(B200_EINVAL, "gemm_f32_reference: null matrix pointer");
+  if (M < 1 || N < 1 || K < 1) return fail(B200_EINVAL, "gemm_f32_reference: invalid shape");
+  const dim3 grid((N + 63) / 64, (M + 63) / 64);
+  b200::ref::gemm_f32_reference_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(A), static_cast<const uint16_t*>(Bm), static_cast<float*>(C),
+      M, N, K, b_col_major);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_f32_reference launch");
   return B200_OK;
 }

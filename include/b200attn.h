@@ -82,6 +82,34 @@ b200_status attention_fwd_scalar(const void* q, const void* k, const void* v, vo
                                  float softmax_scale, b200_stream_t stream);
 
 /*
+ * bf16 GEMM: C[M,N] (bf16, row-major) = A[M,K] (row-major) x B, fp32
+ * accumulation.  b_col_major = 1: B stored [N,K] (column-major B);
+ * b_col_major = 0: B stored [K,N] (row-major, the reference 5.GEMM layout).
+ * Requires K % 8 == 0 and N % 8 == 0 (16-byte rows); any M, N, K >= 1.
+ * Replaces the launch of gemm256_tma_tcgen05_kernel in
+ * 5.GEMM/gemm256_tma_tcgen05_bench.cu:937-956 (benchmark) and :1101-1104
+ * (validation), which take only multiples of 256 and write C as fp32 or not
+ * at all.
+ */
+b200_status gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K,
+                      int b_col_major, b200_stream_t stream);
+
+/*
+ * Comparator: the same product through cublasGemmEx (bf16 in/out, fp32
+ * compute).  Stands in for 6.cuBLAS/cublas_gemm_bench.cu:226-231.
+ */
+b200_status gemm_bf16_cublas(const void* A, const void* B, void* C, int M, int N, int K,
+                             int b_col_major, b200_stream_t stream);
+
+/*
+ * Validation-only fp32 CUDA-core GEMM: C[M,N] fp32 row-major.  GPU analogue
+ * of the reference's double-precision CPU loop
+ * (5.GEMM/gemm256_tma_tcgen05_bench.cu:1115-1137) for full-size checks.
+ */
+b200_status gemm_f32_reference(const void* A, const void* B, void* C, int M, int N, int K,
+                               int b_col_major, b200_stream_t stream);
+
+/*
  * Seeded bf16 generators (counter-based: value = f(seed, tensor_id,
  * index_base + i)), so any shard of a tensor can be generated independently.
  * Stand in for the benchmark fill fill_packed_bf16 (0.attention/attention.cu:142-147,
