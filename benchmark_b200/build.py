@@ -80,7 +80,7 @@ def build_harness(verbose: bool = False, force: bool = False) -> list[Path]:
             built.append(exe)
             continue
         cmd = [nvcc(), "-O2", "-std=c++17", f"-I{INCLUDE}", f"-I{HARNESS_SRC}",
-               f"-I{ROOT / 'oracle'}", "-o", str(exe), str(src),
+               "-o", str(exe), str(src),
                f"-L{PKG}", "-lb200attn", f"-Xlinker=-rpath,$ORIGIN/..", "-lcudart", "-lpthread"]
         _run(cmd, verbose)
         built.append(exe)

@@ -1,0 +1,419 @@
+// attention_bench -- C++ host harness over the C ABI (include/b200attn.h).
+//
+// Mirrors the reference harness 0.attention/main.cu (flags parse_args
+// :1603-1704, modes main :2136-2152) so its runners keep working:
+//   benchmark      --blocks N --k-tiles N --warmup N --iters N --csv PATH
+//                  (blocks 128-row Q tiles over heads of k_tiles*128 keys:
+//                   B=1, H=ceil(blocks/k_tiles), N=k_tiles*128, D=128 unless
+//                   --d/--b/--h override; CSV tail fields in the positions
+//                   0.attention/run.py:32-46 parses: [-21] ms, [-4] total
+//                   TFLOP/s, [-3] status, [-2] cuda_error)
+//   --validate / --validate-suite           fused kernel vs the scalar kernel
+//   --scalar-validate / --scalar-validate-suite   scalar kernel vs the fused
+//   general shape flags --b --hq --hkv --sq --skv --d --causal --scale
+//   --pattern constant|onehot|rank1|random|normal|uniform  --seed --sigma
+//   --checksum-repeats N (outputs must be bit-identical across repeats)
+// Exit codes as the reference: 0 ok, 1 failure, 2 bad arguments, 77 no SM100.
+//
+// Validation compares the two GPU kernels of the library with the harness
+// tolerance (an element fails only when abs > 6e-2 AND rel > 8e-2,
+// main.cu:1929); the CPU oracle comparison lives in the test suite.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "b200attn.h"
+
+namespace {
+
+struct Args {
+  std::string mode = "benchmark";
+  bool suite = false;
+  int blocks = 4096, k_tiles = 256, warmup = 3, iters = 10;
+  int B = 1, Hq = 1, Hkv = 1, Sq = 128, Skv = 128, D = 128, causal = 0;
+  int bench_b = 0, bench_h = 0;  // optional benchmark overrides
+  float scale = -1.0f, sigma = 1.0f;
+  unsigned long long seed = 2024;
+  int checksum_repeats = 2;
+  std::string pattern = "constant";
+  std::string csv;
+};
+
+void usage() {
+  std::printf(
+      "attention_bench [mode] [options]\n"
+      "  benchmark (default): --blocks N --k-tiles N --warmup N --iters N --csv PATH\n"
+      "                       [--d 64|128] [--b N --h N] [--causal] [--pattern P --seed S]\n"
+      "  --validate | --validate-suite          fused kernel vs scalar kernel\n"
+      "  --scalar-validate | --scalar-validate-suite\n"
+      "  --b --hq --hkv --sq --skv --d --causal --no-causal --scale --pattern --seed --sigma\n"
+      "  --checksum-repeats N --csv PATH\n");
+}
+
+bool parse(int argc, char** argv, Args* a) {
+  for (int i = 1; i < argc; ++i) {
+    const std::string f = argv[i];
+    auto next = [&](const char* what) -> const char* {
+      if (i + 1 >= argc) {
+        std::fprintf(stderr, "%s needs a value\n", what);
+        std::exit(2);
+      }
+      return argv[++i];
+    };
+    if (f == "--help" || f == "-h") { usage(); std::exit(0); }
+    else if (f == "--blocks") a->blocks = std::atoi(next("--blocks"));
+    else if (f == "--k-tiles") a->k_tiles = std::atoi(next("--k-tiles"));
+    else if (f == "--warmup") a->warmup = std::atoi(next("--warmup"));
+    else if (f == "--iters") a->iters = std::atoi(next("--iters"));
+    else if (f == "--csv") a->csv = next("--csv");
+    else if (f == "--validate" || f == "--fused-validate" || f == "--real-validate") a->mode = "fused_validate";
+    else if (f == "--validate-suite") { a->mode = "fused_validate"; a->suite = true; }
+    else if (f == "--scalar-validate") a->mode = "scalar_validate";
+    else if (f == "--scalar-validate-suite") { a->mode = "scalar_validate"; a->suite = true; }
+    else if (f == "--b") { a->B = std::atoi(next("--b")); a->bench_b = a->B; }
+    else if (f == "--h") a->bench_h = std::atoi(next("--h"));
+    else if (f == "--hq") a->Hq = std::atoi(next("--hq"));
+    else if (f == "--hkv") a->Hkv = std::atoi(next("--hkv"));
+    else if (f == "--sq") a->Sq = std::atoi(next("--sq"));
+    else if (f == "--skv") a->Skv = std::atoi(next("--skv"));
+    else if (f == "--d") a->D = std::atoi(next("--d"));
+    else if (f == "--causal") a->causal = 1;
+    else if (f == "--no-causal") a->causal = 0;
+    else if (f == "--scale") a->scale = static_cast<float>(std::atof(next("--scale")));
+    else if (f == "--sigma") a->sigma = static_cast<float>(std::atof(next("--sigma")));
+    else if (f == "--seed") a->seed = std::strtoull(next("--seed"), nullptr, 10);
+    else if (f == "--pattern") a->pattern = next("--pattern");
+    else if (f == "--checksum-repeats") a->checksum_repeats = std::atoi(next("--checksum-repeats"));
+    else {
+      std::fprintf(stderr, "unknown argument %s\n", argv[i]);
+      usage();
+      return false;
+    }
+  }
+  if (a->blocks < 1 || a->k_tiles < 1 || a->warmup < 0 || a->iters < 1) {
+    std::fprintf(stderr, "invalid benchmark shape or counts\n");
+    return false;
+  }
+  if (a->D != 64 && a->D != 128) {
+    std::fprintf(stderr, "--d must be 64 or 128\n");
+    return false;
+  }
+  const std::string& p = a->pattern;
+  if (p != "constant" && p != "onehot" && p != "rank1" && p != "random" && p != "normal" &&
+      p != "uniform") {
+    std::fprintf(stderr, "unknown pattern %s\n", p.c_str());
+    return false;
+  }
+  return true;
+}
+
+// ---- input patterns (the harness's deterministic fills) ----
+uint16_t to_bf16(float v) {
+  uint32_t b;
+  std::memcpy(&b, &v, 4);
+  b += 0x7fffu + ((b >> 16) & 1u);
+  return static_cast<uint16_t>(b >> 16);
+}
+
+float bf16_to_f32(uint16_t h) {
+  const uint32_t w = static_cast<uint32_t>(h) << 16;
+  float f;
+  std::memcpy(&f, &w, 4);
+  return f;
+}
+
+uint32_t mix32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+
+// Same value definitions as the reference's validation patterns
+// (0.attention/main.cu:1266-1306).
+float pattern_value(const std::string& pat, char m, int b, int h, int s, int d) {
+  if (pat == "constant") return m == 'v' ? 0.125f : 0.0625f;
+  if (pat == "onehot") {
+    if (m != 'v') return d == (s & 127) ? 1.0f : 0.0f;
+    return d == ((s + h) & 127) ? 0.5f : 0.0f;
+  }
+  if (pat == "rank1") {
+    const float ss = static_cast<float>((s % 17) + 1) * 0.0078125f;
+    const float ds = static_cast<float>((d % 19) + 1) * 0.00390625f;
+    const float hs = static_cast<float>((h % 7) + 1) * 0.0009765625f;
+    return m == 'v' ? 0.5f * ss + ds + hs : ss + ds + hs;
+  }
+  const uint32_t tag = m == 'q' ? 0x1234u : (m == 'k' ? 0x5678u : 0x9abcu);
+  const uint32_t x = tag ^ (static_cast<uint32_t>(b) * 131071u + static_cast<uint32_t>(h) * 8191u +
+                            static_cast<uint32_t>(s) * 257u + static_cast<uint32_t>(d));
+  const float u = static_cast<float>(mix32(x) & 0xffffu) * (1.0f / 65535.0f);
+  return (m == 'v' ? 0.5f : 0.25f) * (u * 2.0f - 1.0f);
+}
+
+struct Dev {
+  void* p = nullptr;
+  explicit Dev(size_t bytes) {
+    if (cudaMalloc(&p, bytes) != cudaSuccess) p = nullptr;
+  }
+  ~Dev() {
+    if (p) cudaFree(p);
+  }
+};
+
+bool fill(void* dst, char m, int B, int H, int S, int D, const Args& a, uint32_t tid) {
+  const size_t n = static_cast<size_t>(B) * H * S * D;
+  if (a.pattern == "normal")
+    return b200_fill_normal_bf16(dst, n, a.seed, tid, 0, 0.0f, a.sigma, nullptr) == B200_OK;
+  if (a.pattern == "uniform")
+    return b200_fill_uniform_bf16(dst, n, a.seed, tid, 0, -a.sigma, a.sigma, nullptr) == B200_OK;
+  std::vector<uint16_t> h(n);
+  for (int b = 0; b < B; ++b)
+    for (int hh = 0; hh < H; ++hh)
+      for (int s = 0; s < S; ++s)
+        for (int d = 0; d < D; ++d)
+          h[((static_cast<size_t>(b) * H + hh) * S + s) * D + d] =
+              to_bf16(pattern_value(a.pattern, m, b, hh, s, d));
+  return cudaMemcpy(dst, h.data(), n * 2, cudaMemcpyHostToDevice) == cudaSuccess;
+}
+
+uint64_t fnv1a(const void* data, size_t bytes) {
+  const uint8_t* p = static_cast<const uint8_t*>(data);
+  uint64_t h = 1469598103934665603ull;
+  for (size_t i = 0; i < bytes; ++i) {
+    h ^= p[i];
+    h *= 1099511628211ull;
+  }
+  return h;
+}
+
+struct CaseResult {
+  std::string stage;
+  bool ok = false;
+  float max_abs = 0, max_rel = 0;
+  size_t bad = 0;
+  uint64_t checksum = 0, repeat_checksum = 0;
+  bool stable = true;
+};
+
+// One validation case: `primary` (the kernel under test) against `other`.
+CaseResult run_case(const Args& a, const std::string& label, bool fused_primary) {
+  CaseResult r;
+  char stage[256];
+  std::snprintf(stage, sizeof(stage), "%s_B%d_Hq%d_Hkv%d_Sq%d_Skv%d_D%d_%s_pattern_%s",
+                label.c_str(), a.B, a.Hq, a.Hkv, a.Sq, a.Skv, a.D,
+                a.causal ? "causal" : "noncausal", a.pattern.c_str());
+  r.stage = stage;
+  const size_t nq = static_cast<size_t>(a.B) * a.Hq * a.Sq * a.D;
+  const size_t nkv = static_cast<size_t>(a.B) * a.Hkv * a.Skv * a.D;
+  Dev q(nq * 2), k(nkv * 2), v(nkv * 2), o1(nq * 2), o2(nq * 2);
+  if (!q.p || !k.p || !v.p || !o1.p || !o2.p) return r;
+  if (!fill(q.p, 'q', a.B, a.Hq, a.Sq, a.D, a, 0) || !fill(k.p, 'k', a.B, a.Hkv, a.Skv, a.D, a, 1) ||
+      !fill(v.p, 'v', a.B, a.Hkv, a.Skv, a.D, a, 2))
+    return r;
+  auto fused = [&](void* o) {
+    return attention_fwd(q.p, k.p, v.p, o, a.B, a.Hq, a.Hkv, a.Sq, a.Skv, a.D, a.causal, a.scale,
+                         nullptr);
+  };
+  auto scalar = [&](void* o) {
+    return attention_fwd_scalar(q.p, k.p, v.p, o, a.B, a.Hq, a.Hkv, a.Sq, a.Skv, a.D, a.causal,
+                                a.scale, nullptr);
+  };
+  std::vector<uint16_t> h1(nq), h2(nq);
+  const int reps = std::max(1, a.checksum_repeats);
+  for (int rep = 0; rep < reps; ++rep) {
+    b200_status st = fused_primary ? fused(o1.p) : scalar(o1.p);
+    if (st == B200_OK) st = fused_primary ? scalar(o2.p) : fused(o2.p);
+    if (st == B200_OK) st = b200_check(nullptr);
+    if (st != B200_OK) {
+      std::fprintf(stderr, "%s: %s\n", r.stage.c_str(), b200_last_error());
+      return r;
+    }
+    cudaMemcpy(h1.data(), o1.p, nq * 2, cudaMemcpyDeviceToHost);
+    cudaMemcpy(h2.data(), o2.p, nq * 2, cudaMemcpyDeviceToHost);
+    const uint64_t cs = fnv1a(h1.data(), nq * 2);
+    if (rep == 0) r.checksum = cs;
+    r.repeat_checksum = cs;
+    r.stable = r.stable && cs == r.checksum;
+  }
+  r.ok = true;
+  for (size_t i = 0; i < nq; ++i) {
+    const float g = bf16_to_f32(h1[i]), e = bf16_to_f32(h2[i]);
+    const float diff = std::fabs(g - e);
+    const float rel = diff / std::max(std::fabs(e), 1.0e-6f);
+    r.max_abs = std::max(r.max_abs, diff);
+    r.max_rel = std::max(r.max_rel, rel);
+    if (!std::isfinite(g) || (diff > 6.0e-2f && rel > 8.0e-2f)) {
+      r.ok = false;
+      ++r.bad;
+    }
+  }
+  r.ok = r.ok && r.stable;
+  return r;
+}
+
+int run_validation(const Args& a) {
+  const bool fused_primary = a.mode == "fused_validate";
+  std::vector<CaseResult> results;
+  if (a.suite) {
+    struct Case {
+      int B, Hq, Hkv, Sq, Skv, causal;
+      const char* pattern;
+      const char* label;
+    };
+    // The reference's fused suite (main.cu:1942-1947) and scalar suite
+    // (main.cu:1998-2005); both kernels accept every shape here.
+    const Case cases[] = {
+        {1, 1, 1, 128, 128, 0, "constant", "constant_k1"},
+        {1, 1, 1, 128, 512, 0, "rank1", "rank1_k4"},
+        {1, 1, 1, 128, 512, 0, "random", "random_k4"},
+        {1, 1, 1, 128, 1024, 0, "random", "random_k8"},
+        {1, 1, 1, 128, 256, 0, "rank1", "rank1_multi_k"},
+        {1, 1, 1, 128, 384, 1, "rank1", "causal_k_longer"},
+        {1, 1, 1, 77, 193, 0, "random", "random_tail"},
+        {2, 4, 4, 128, 256, 0, "random", "b2_h4"},
+        {1, 8, 2, 64, 128, 0, "random", "gqa"},
+    };
+    for (const Case& c : cases) {
+      Args ca = a;
+      ca.B = c.B;
+      ca.Hq = c.Hq;
+      ca.Hkv = c.Hkv;
+      ca.Sq = c.Sq;
+      ca.Skv = c.Skv;
+      ca.causal = c.causal;
+      ca.pattern = c.pattern;
+      results.push_back(run_case(ca, c.label, fused_primary));
+    }
+  } else {
+    results.push_back(run_case(a, "real_attention", fused_primary));
+  }
+  FILE* csv = a.csv.empty() ? nullptr : std::fopen(a.csv.c_str(), "w");
+  if (csv)
+    std::fprintf(csv, "stage,status,max_abs,max_rel,bad_count,checksum,repeat_checksum,"
+                      "checksum_stable\n");
+  bool all = true;
+  for (const CaseResult& r : results) {
+    all = all && r.ok;
+    std::printf("%s status=%s max_abs=%g max_rel=%g bad=%zu checksum=%016llx "
+                "repeat_checksum=%016llx checksum_stable=%s\n",
+                r.stage.c_str(), r.ok ? "ok" : "fail", r.max_abs, r.max_rel, r.bad,
+                static_cast<unsigned long long>(r.checksum),
+                static_cast<unsigned long long>(r.repeat_checksum), r.stable ? "yes" : "no");
+    if (csv)
+      std::fprintf(csv, "%s,%s,%g,%g,%zu,%016llx,%016llx,%s\n", r.stage.c_str(),
+                   r.ok ? "ok" : "fail", r.max_abs, r.max_rel, r.bad,
+                   static_cast<unsigned long long>(r.checksum),
+                   static_cast<unsigned long long>(r.repeat_checksum), r.stable ? "yes" : "no");
+  }
+  if (csv) std::fclose(csv);
+  return all ? 0 : 1;
+}
+
+int run_benchmark(const Args& a) {
+  const int H = a.bench_h > 0 ? a.bench_h : (a.blocks + a.k_tiles - 1) / a.k_tiles;
+  const int B = a.bench_b > 0 ? a.bench_b : 1;
+  const int N = a.k_tiles * 128, D = a.D;
+  const size_t n = static_cast<size_t>(B) * H * N * D;
+  Dev q(n * 2), k(n * 2), v(n * 2), o(n * 2);
+  const char* status = "ok";
+  cudaError_t cerr = cudaSuccess;
+  float ms = 0, mn = 1e30f, mx = 0;
+  if (!q.p || !k.p || !v.p || !o.p) {
+    status = "alloc_failed";
+    cerr = cudaGetLastError();
+  } else {
+    Args fa = a;
+    if (fa.pattern == "constant") fa.pattern = "normal";  // benchmark data: seeded N(0, sigma)
+    if (!fill(q.p, 'q', B, H, N, D, fa, 0) || !fill(k.p, 'k', B, H, N, D, fa, 1) ||
+        !fill(v.p, 'v', B, H, N, D, fa, 2))
+      status = "fill_failed";
+  }
+  auto launch = [&]() {
+    return attention_fwd(q.p, k.p, v.p, o.p, B, H, H, N, N, D, a.causal, a.scale, nullptr);
+  };
+  if (std::strcmp(status, "ok") == 0) {
+    for (int i = 0; i < a.warmup; ++i)
+      if (launch() != B200_OK) status = "warmup_launch_failed";
+    if (b200_check(nullptr) != B200_OK) status = "warmup_runtime_failed";
+  }
+  if (std::strcmp(status, "ok") == 0) {
+    cudaEvent_t e0, e1, t0, t1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventCreate(&t0);
+    cudaEventCreate(&t1);
+    cudaEventRecord(e0);
+    for (int i = 0; i < a.iters; ++i) {
+      cudaEventRecord(t0);
+      if (launch() != B200_OK) status = "timed_launch_failed";
+      cudaEventRecord(t1);
+      cudaEventSynchronize(t1);
+      float one = 0;
+      cudaEventElapsedTime(&one, t0, t1);
+      mn = std::min(mn, one);
+      mx = std::max(mx, one);
+    }
+    cudaEventRecord(e1);
+    cudaEventSynchronize(e1);
+    cudaEventElapsedTime(&ms, e0, e1);
+    ms /= static_cast<float>(a.iters);
+    if (b200_check(nullptr) != B200_OK) status = "timed_runtime_failed";
+    cerr = cudaGetLastError();
+  }
+  const double flops = 4.0 * B * H * static_cast<double>(N) * N * D * (a.causal ? 0.5 : 1.0);
+  const double tflops = ms > 0 ? flops / (ms * 1e-3) / 1e12 : 0.0;
+  const double gb = static_cast<double>(n) * 2 / 1e9;  // one tensor
+  auto tbps = [&](double g) { return ms > 0 ? g / (ms * 1e-3) / 1e3 : 0.0; };
+  char header[1024];
+  std::snprintf(header, sizeof(header),
+                "mode,B,H,N,D,causal,blocks,k_tiles,warmup,iters,threads_per_cta,elapsed_ms,"
+                "q_GB,k_GB,v_GB,o_GB,total_GB,q_TBps,k_TBps,v_TBps,o_TBps,total_TBps,min_ms,"
+                "max_ms,flops,qk_TFLOP_per_s,pv_TFLOP_per_s,bf16_peak_fraction,"
+                "total_TFLOP_per_s,status,cuda_error,notes\n");
+  char row[2048];
+  std::snprintf(row, sizeof(row),
+                "b200_fused_attention,%d,%d,%d,%d,%d,%d,%d,%d,%d,320,%.6f,%.6f,%.6f,%.6f,%.6f,"
+                "%.6f,%.3f,%.3f,%.3f,%.3f,%.3f,%.6f,%.6f,%.0f,%.3f,%.3f,%.4f,%.3f,%s,%s,%s\n",
+                B, H, N, D, a.causal, a.blocks, a.k_tiles, a.warmup, a.iters, ms, gb, gb, gb, gb,
+                4 * gb, tbps(gb), tbps(gb), tbps(gb), tbps(gb), tbps(4 * gb), mn, mx, flops,
+                tflops / 2, tflops / 2, tflops / 1613.4, tflops, status,
+                cudaGetErrorString(cerr), "seeded_normal_inputs");
+  if (!a.csv.empty()) {
+    FILE* f = std::fopen(a.csv.c_str(), "w");
+    if (f) {
+      std::fputs(header, f);
+      std::fputs(row, f);
+      std::fclose(f);
+    }
+  }
+  std::printf("%s%s", header, row);
+  return std::strcmp(status, "ok") == 0 ? 0 : 1;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  Args a;
+  if (!parse(argc, argv, &a)) return 2;
+  int dev = 0;
+  cudaDeviceProp prop{};
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+    std::fprintf(stderr, "no CUDA device\n");
+    return 77;
+  }
+  if (prop.major < 10) {
+    std::fprintf(stderr, "this build requires sm_100a; got sm_%d%d\n", prop.major, prop.minor);
+    return 77;
+  }
+  if (a.mode == "benchmark") return run_benchmark(a);
+  return run_validation(a);
+}

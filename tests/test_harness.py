@@ -1,0 +1,77 @@
+"""The C++ host harnesses (benchmark_b200/harness) mirror the reference's
+bench CLIs: 0.attention/main.cu (exit codes 0 ok, 1 failure, 2 bad
+arguments, 77 no usable GPU) and 5.GEMM/gemm256_tma_tcgen05_bench.cu.
+CPU tests check argument handling; GPU tests run their validation modes."""
+import csv
+import subprocess
+from pathlib import Path
+
+import pytest
+
+BIN = Path(__file__).resolve().parents[1] / "benchmark_b200" / "bin"
+ATTN = BIN / "attention_bench"
+GEMM = BIN / "gemm_bench"
+
+
+def _run(exe, *args, timeout=600):
+    if not exe.exists():
+        pytest.fail(f"{exe.name} is not built (python -m benchmark_b200.build)")
+    return subprocess.run([str(exe), *args], capture_output=True, text=True, timeout=timeout)
+
+
+@pytest.mark.parametrize("exe", [ATTN, GEMM])
+def test_help_exits_zero(exe):
+    r = _run(exe, "--help")
+    assert r.returncode == 0 and "--" in r.stdout
+
+
+@pytest.mark.parametrize("args", [["--bogus"], ["--d", "96"], ["--iters", "0"],
+                                  ["--blocks", "-1"], ["--pattern", "zebra"]])
+def test_attention_bad_arguments_exit_two(args):
+    assert _run(ATTN, *args).returncode == 2
+
+
+@pytest.mark.parametrize("args", [["--bogus"], ["--sizes", "100"], ["--impl", "x"],
+                                  ["--validate-pattern", "zebra"], ["--b-layout", "diag"]])
+def test_gemm_bad_arguments_exit_two(args):
+    assert _run(GEMM, *args).returncode == 2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["--validate-suite", "--scalar-validate-suite"])
+def test_attention_validate_suite(mode):
+    r = _run(ATTN, mode)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+@pytest.mark.gpu
+def test_attention_benchmark_csv(tmp_path):
+    out = tmp_path / "attn.csv"
+    r = _run(ATTN, "--blocks", "8", "--k-tiles", "4", "--warmup", "1", "--iters", "2",
+             "--csv", str(out))
+    assert r.returncode == 0, r.stderr
+    rows = list(csv.reader(out.open()))
+    assert len(rows) == 2
+    # run.py reads the tail of each row: TFLOP/s, status, cuda_error, notes.
+    assert rows[1][-3] == "ok" and float(rows[1][-4]) > 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("impl", ["tcgen05", "cublas"])
+@pytest.mark.parametrize("layout", ["col", "row"])
+@pytest.mark.parametrize("pattern,size", [("pattern", "256"), ("ones", "512"),
+                                          ("pattern", "1024")])
+def test_gemm_validate(impl, layout, pattern, size):
+    r = _run(GEMM, "--validate", "--validate-size", size, "--validate-pattern", pattern,
+             "--impl", impl, "--b-layout", layout)
+    assert r.returncode == 0 and "status=ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.gpu
+def test_gemm_benchmark_csv(tmp_path):
+    out = tmp_path / "gemm.csv"
+    r = _run(GEMM, "--sizes", "1024,2048", "--warmup", "1", "--iters", "2", "--csv", str(out))
+    assert r.returncode == 0, r.stdout + r.stderr
+    rows = list(csv.DictReader(out.open()))
+    assert [int(x["size"]) for x in rows] == [1024, 2048]
+    assert all(x["status"] == "ok" and float(x["event_TFLOPS"]) > 0 for x in rows)
