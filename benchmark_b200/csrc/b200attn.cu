@@ -396,37 +396,115 @@ extern "C" b200_status b200_selftest_wait_timeout(uint64_t limit_ns, b200_stream
   return B200_OK;
 }
 
-extern "C" b200_status gemm_bf16(const void* A, const void* Bm, void* C, int M, int N, int K,
-                                 int b_col_major, b200_stream_t stream) {
-  b200_status st = check_gemm_args(A, Bm, C, M, N, K, "gemm_bf16");
-  if (st != B200_OK) return st;
-  static unsigned attr_done = 0;
-  st = ensure_smem_attr(b200::gemm::gemm_bf16_kernel, b200::gemm::kSmemBytes, &attr_done);
-  if (st != B200_OK) return st;
-  CUtensorMap am, bm;
-  if ((st = encode_bf16_2d(&am, A, K, M, b200::gemm::kBK, b200::gemm::kBM)) != B200_OK) return st;
-  if (b_col_major)
-    st = encode_bf16_2d(&bm, Bm, K, N, b200::gemm::kBK, b200::gemm::kBN);
-  else
-    st = encode_bf16_2d(&bm, Bm, N, K, 64, b200::gemm::kBK);
-  if (st != B200_OK) return st;
+namespace {
+
+// Which tcgen05 GEMM kernel gemm_bf16 runs: the CTA-pair 256x256 kernel
+// (default) or the single-CTA 128x256 kernel.  B200_GEMM_KERNEL=single|pair
+// selects one for comparisons.
+bool gemm_use_pair() {
+  static const bool pair = [] {
+    const char* e = std::getenv("B200_GEMM_KERNEL");
+    return !(e && std::strcmp(e, "single") == 0);
+  }();
+  return pair;
+}
+
+b200::gemm::Params gemm_params(int M, int N, int K, int b_col_major, void* C, int bm, int bn,
+                               int bk) {
   b200::gemm::Params p{};
   p.M = M;
   p.N = N;
   p.K = K;
-  p.tiles_m = (M + b200::gemm::kBM - 1) / b200::gemm::kBM;
-  p.tiles_n = (N + b200::gemm::kBN - 1) / b200::gemm::kBN;
-  p.k_blocks = (K + b200::gemm::kBK - 1) / b200::gemm::kBK;
+  p.tiles_m = (M + bm - 1) / bm;
+  p.tiles_n = (N + bn - 1) / bn;
+  p.k_blocks = (K + bk - 1) / bk;
   p.b_col_major = b_col_major ? 1 : 0;
   p.C = static_cast<uint16_t*>(C);
+  return p;
+}
+
+b200_status launch_gemm_single(const void* A, const void* Bm, void* C, int M, int N, int K,
+                               int b_col_major, cudaStream_t stream) {
+  namespace g = b200::gemm;
+  static unsigned attr_done = 0;
+  b200_status st = ensure_smem_attr(g::gemm_bf16_kernel, g::kSmemBytes, &attr_done);
+  if (st != B200_OK) return st;
+  CUtensorMap am, bm;
+  if ((st = encode_bf16_2d(&am, A, K, M, g::kBK, g::kBM)) != B200_OK) return st;
+  if (b_col_major)
+    st = encode_bf16_2d(&bm, Bm, K, N, g::kBK, g::kBN);
+  else
+    st = encode_bf16_2d(&bm, Bm, N, K, 64, g::kBK);
+  if (st != B200_OK) return st;
+  const g::Params p = gemm_params(M, N, K, b_col_major, C, g::kBM, g::kBN, g::kBK);
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
   if (tiles > 0x7fffffffll) return fail(B200_EUNSUPPORTED, "gemm_bf16: too many tiles");
   const int grid = static_cast<int>(std::min<long long>(tiles, sm_count()));
-  b200::gemm::gemm_bf16_kernel<<<grid, b200::gemm::kThreads, b200::gemm::kSmemBytes,
-                                 reinterpret_cast<cudaStream_t>(stream)>>>(am, bm, p);
+  g::gemm_bf16_kernel<<<grid, g::kThreads, g::kSmemBytes, stream>>>(am, bm, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16 launch");
   return B200_OK;
+}
+
+// Clusters of two that can be resident at once on the current device.
+int pair_clusters_resident() {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+  cfg.blockDim = dim3(b200::gemm::pair::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = b200::gemm::pair::kSmemBytes;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, b200::gemm::gemm_bf16_pair_kernel, &cfg) !=
+          cudaSuccess ||
+      n < 1) {
+    cudaGetLastError();
+    n = sm_count() / 2;
+  }
+  cache[dev] = n;
+  return n;
+}
+
+b200_status launch_gemm_pair(const void* A, const void* Bm, void* C, int M, int N, int K,
+                             int b_col_major, cudaStream_t stream) {
+  namespace g = b200::gemm;
+  static unsigned attr_done = 0;
+  b200_status st = ensure_smem_attr(g::gemm_bf16_pair_kernel, g::pair::kSmemBytes, &attr_done);
+  if (st != B200_OK) return st;
+  CUtensorMap am, bm;
+  // Each CTA of a pair loads 128-row halves of the 256-row A and B tiles.
+  if ((st = encode_bf16_2d(&am, A, K, M, g::pair::kBK, g::pair::kHalf)) != B200_OK) return st;
+  if (b_col_major)
+    st = encode_bf16_2d(&bm, Bm, K, N, g::pair::kBK, g::pair::kHalf);
+  else
+    st = encode_bf16_2d(&bm, Bm, N, K, 64, g::pair::kBK);
+  if (st != B200_OK) return st;
+  const g::Params p = gemm_params(M, N, K, b_col_major, C, g::pair::kBM, g::pair::kBN,
+                                  g::pair::kBK);
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  if (tiles > 0x3fffffffll) return fail(B200_EUNSUPPORTED, "gemm_bf16: too many tiles");
+  const long long clusters = std::min<long long>(tiles, pair_clusters_resident());
+  g::gemm_bf16_pair_kernel<<<static_cast<unsigned>(2 * clusters), g::pair::kThreads,
+                             g::pair::kSmemBytes, stream>>>(am, bm, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16 (pair) launch");
+  return B200_OK;
+}
+
+}  // namespace
+
+extern "C" b200_status gemm_bf16(const void* A, const void* Bm, void* C, int M, int N, int K,
+                                 int b_col_major, b200_stream_t stream) {
+  const b200_status st = check_gemm_args(A, Bm, C, M, N, K, "gemm_bf16");
+  if (st != B200_OK) return st;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return gemm_use_pair() ? launch_gemm_pair(A, Bm, C, M, N, K, b_col_major, s)
+                         : launch_gemm_single(A, Bm, C, M, N, K, b_col_major, s);
 }
 
 extern "C" b200_status gemm_bf16_cublas(const void* A, const void* Bm, void* C, int M, int N,

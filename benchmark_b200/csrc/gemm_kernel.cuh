@@ -51,12 +51,14 @@ struct Params {
   uint16_t* C;
 };
 
-// Tile t -> (m block, n block) in groups of kGroupM row blocks.
-__device__ __forceinline__ void tile_coords(const Params& p, int t, int* mb, int* nb) {
-  const int per_group = kGroupM * p.tiles_n;
+// Tile t -> (m block, n block) in groups of `group` row blocks: a group's
+// tiles walk its row blocks fastest, so the CTAs running at one time share
+// a few B column blocks and a few A row blocks while they sit in L2.
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int group, int* mb, int* nb) {
+  const int per_group = group * p.tiles_n;
   const int g = t / per_group;
-  const int first_m = g * kGroupM;
-  const int gsize = min(kGroupM, p.tiles_m - first_m);
+  const int first_m = g * group;
+  const int gsize = min(group, p.tiles_m - first_m);
   const int r = t - g * per_group;
   *mb = first_m + r % gsize;
   *nb = r / gsize;
@@ -120,7 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int mb, nb;
-        tile_coords(p, t, &mb, &nb);
+        tile_coords(p, t, kGroupM, &mb, &nb);
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = static_cast<uint32_t>(it / kStages) & 1u;
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
       const int a = lt & 1;
       int mb, nb;
-      tile_coords(p, t, &mb, &nb);
+      tile_coords(p, t, kGroupM, &mb, &nb);
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[a],
                                                         static_cast<uint32_t>(lt >> 1) & 1u,
                                                         kSiteAccFull));
@@ -232,6 +234,237 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+
+// ===========================================================================
+// CTA-pair variant: 256x256 output tiles per cluster of two CTAs
+// (tcgen05 cta_group::2, the reference's 256x256 CTA tile).
+//
+// Each CTA of the pair loads its 128 rows of A and its 128 rows (N) of B per
+// 64-deep K stage; the even CTA issues M=256, N=256, K=16 MMAs that read both
+// CTAs' shared memory and leave 128 accumulator rows in each CTA's TMEM.  Per
+// SM and per stage that is 32 KiB of TMA traffic for 2 x 128x256x64 MACs,
+// half the B bytes of the single-CTA 128x256 tile.  No copy is multicast:
+// each CTA fetches its own halves.
+//
+//   warp 0 (both CTAs): TMA producer; both count their bytes on the even
+//                       CTA's full[s] barrier, which the even CTA arms with
+//                       the pair's total
+//   warp 1 (even CTA):  MMA issuer; commits free the stage (empty[s]) and
+//                       publish the accumulator (acc_full[a]) in both CTAs
+//   warps 2-5 (both):   epilogue of this CTA's 128 rows; one arrive per warp
+//                       on the even CTA's acc_empty[a] (8 per tile)
+// ===========================================================================
+namespace pair {
+constexpr int kBM = 256;  // output rows per pair tile (128 per CTA)
+constexpr int kBN = 256;  // output columns per pair tile (128 B rows per CTA)
+constexpr int kHalf = 128;
+constexpr int kBK = 64;
+constexpr int kStages = 6;
+constexpr int kThreads = 192;
+constexpr int kTmaWarp = 0;
+constexpr int kMmaWarp = 1;
+constexpr int kGroupM = 8;
+constexpr uint32_t kTmemCols = 512;  // two accumulators of 256 fp32 columns
+constexpr int kABytes = kHalf * kBK * 2;        // 16 KiB
+constexpr int kBBytes = kHalf * kBK * 2;        // 16 KiB
+constexpr int kStageBytes = kABytes + kBBytes;  // 32 KiB
+constexpr int kBarOff = kStages * kStageBytes;
+constexpr int kNumBars = 2 * kStages + 5;  // full, empty, acc_full[2], acc_empty[2], drain
+constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
+constexpr int kSmemBytes = kTmemSlotOff + 16 + 1024;
+constexpr uint32_t kAccEmptyArrivals = 8;  // 4 epilogue warps x 2 CTAs
+}  // namespace pair
+
+__device__ __forceinline__ void spin_ns(uint64_t ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < ns) __nanosleep(1000);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap a_map,
+                          const __grid_constant__ CUtensorMap b_map, const Params p) {
+  // the pair tile's constants shadow the single-CTA ones inside this kernel
+  constexpr int kBM = pair::kBM, kBN = pair::kBN, kHalf = pair::kHalf, kBK = pair::kBK;
+  constexpr int kStages = pair::kStages, kTmaWarp = pair::kTmaWarp, kMmaWarp = pair::kMmaWarp;
+  constexpr int kGroupM = pair::kGroupM, kABytes = pair::kABytes;
+  constexpr int kStageBytes = pair::kStageBytes, kBarOff = pair::kBarOff;
+  constexpr int kTmemSlotOff = pair::kTmemSlotOff;
+  constexpr uint32_t kTmemCols = pair::kTmemCols;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTmemSlotOff);
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+  const int num_clusters = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], pair::kAccEmptyArrivals);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (warp == kTmaWarp && lane == 0) {
+    tma_prefetch_desc(&a_map);
+    tma_prefetch_desc(&b_map);
+  }
+  // Both CTAs' barriers are initialised before either touches the other's.
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == kTmaWarp) {
+    // ================= TMA producer (both CTAs) =================
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_last();
+      int it = 0, issued_last = -1;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        int mb, nb;
+        tile_coords(p, t, kGroupM, &mb, &nb);
+        const int arow = mb * kBM + static_cast<int>(rank) * kHalf;
+        const int brow = nb * kBN + static_cast<int>(rank) * kHalf;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = static_cast<uint32_t>(it / kStages) & 1u;
+          ok = mbar_wait(&empty[s], ph ^ 1u, kSiteEmpty);
+          if (!ok) break;
+          uint8_t* sa = smem + s * kStageBytes;
+          uint8_t* sb = sa + kABytes;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * kStageBytes);
+          const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+          tma_load_2d_pair(sa, &a_map, fb, kb * kBK, arow, pol);
+          if (p.b_col_major) {
+            tma_load_2d_pair(sb, &b_map, fb, kb * kBK, brow, pol);
+          } else {
+#pragma unroll
+            for (int h = 0; h < kHalf / 64; ++h)
+              tma_load_2d_pair(sb + h * (kBK * 128), &b_map, fb, brow + h * 64, kb * kBK, pol);
+          }
+          issued_last = it;
+        }
+      }
+      if (!ok) {
+        // Unwinding: let the copies already issued land before the pair exits.
+        if (leader) {
+          for (int i = max(0, issued_last - kStages + 1); i <= issued_last; ++i)
+            drain_wait(&full[i % kStages], static_cast<uint32_t>(i / kStages) & 1u);
+        } else {
+          spin_ns(200000);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ================= MMA issuer (even CTA) =================
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc_k = idesc_bf16_f32(kBM, kBN, false, false);
+      constexpr uint32_t idesc_mn = idesc_bf16_f32(kBM, kBN, false, true);
+      const uint32_t idesc = p.b_col_major ? idesc_k : idesc_mn;
+      const uint64_t da0 = sdesc_sw128(smem_u32(smem), 16, 1024);
+      const uint64_t db0 = p.b_col_major ? sdesc_sw128(smem_u32(smem) + kABytes, 16, 1024)
+                                         : sdesc_sw128(smem_u32(smem) + kABytes, kBK * 128, 1024);
+      const uint32_t b_step = p.b_col_major ? 2u : (16u * 128u) >> 4;
+      int it = 0, lt = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++lt) {
+        const int a = lt & 1;
+        ok = mbar_wait(&acc_empty[a], (static_cast<uint32_t>(lt >> 1) & 1u) ^ 1u, kSiteAccEmpty);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(a * kBN);
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % kStages;
+          ok = mbar_wait(&full[s], static_cast<uint32_t>(it / kStages) & 1u, kSiteFull);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t da = da0 + s * (kStageBytes >> 4);
+          const uint64_t db = db0 + s * (kStageBytes >> 4);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            mma_ss_pair(d_tmem, da + k * 2, db + k * b_step, idesc, (kb | k) > 0 ? 1u : 0u);
+          mma_commit_pair_both(&empty[s], 0x3);
+        }
+        if (!ok) break;
+        mma_commit_pair_both(&acc_full[a], 0x3);
+      }
+      mma_commit_pair_local(drain);
+      drain_wait(drain, 0);
+    }
+    __syncwarp();
+  } else {
+    // ================= epilogue (warps 2-5, both CTAs) =================
+    const uint32_t quad = warp & 3u;
+    const int row = static_cast<int>(quad * 32 + lane);
+    const uint32_t lane_addr = (quad * 32u) << 16;
+    int lt = 0;
+    for (int t = cluster_id; t < num_tiles; t += num_clusters, ++lt) {
+      const int a = lt & 1;
+      int mb, nb;
+      tile_coords(p, t, kGroupM, &mb, &nb);
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[a],
+                                                        static_cast<uint32_t>(lt >> 1) & 1u,
+                                                        kSiteAccFull));
+      if (!ok) break;
+      tc_fence_after();
+      const int grow = mb * kBM + static_cast<int>(rank) * kHalf + row;
+      uint16_t* crow = p.C + static_cast<size_t>(grow) * p.N;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(a * kBN + c0), v);
+        tmem_wait_ld();
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          w[e] = pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
+        const int gcol = nb * kBN + c0;
+        if (grow < p.M) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (gcol + q * 8 < p.N)
+              *reinterpret_cast<uint4*>(crow + gcol + q * 8) =
+                  make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[a]), 0));
+    }
+  }
+
+  // No CTA leaves while its partner may still signal its barriers or read
+  // its shared memory.
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 

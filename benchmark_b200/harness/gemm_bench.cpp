@@ -177,13 +177,11 @@ int run_bench(const Args& a) {
     if (std::strcmp(status, "ok") == 0) {
       for (int i = 0; i < a.warmup; ++i)
         if (gemm(a, dA, dB, dC, s, s, s) != B200_OK) status = "warmup_failed";
-      cudaEvent_t e0, e1, t0, t1;
-      cudaEventCreate(&e0);
-      cudaEventCreate(&e1);
+      cudaEvent_t t0, t1;
       cudaEventCreate(&t0);
       cudaEventCreate(&t1);
       cudaDeviceSynchronize();
-      cudaEventRecord(e0);
+      // event_ms: mean of per-launch event times; min_ms: fastest launch
       for (int i = 0; i < a.iters; ++i) {
         cudaEventRecord(t0);
         if (gemm(a, dA, dB, dC, s, s, s) != B200_OK) status = "timed_failed";
@@ -192,12 +190,12 @@ int run_bench(const Args& a) {
         float one = 0;
         cudaEventElapsedTime(&one, t0, t1);
         mn = std::min(mn, one);
+        ms += one;
       }
-      cudaEventRecord(e1);
-      cudaEventSynchronize(e1);
-      cudaEventElapsedTime(&ms, e0, e1);
       ms /= static_cast<float>(a.iters);
       if (b200_check(nullptr) != B200_OK) status = "runtime_failed";
+      cudaEventDestroy(t0);
+      cudaEventDestroy(t1);
     }
     const double tflops = ms > 0 ? 2.0 * s * static_cast<double>(s) * s / (ms * 1e-3) / 1e12 : 0;
     std::printf("size=%d impl=%s b_layout=%s event_ms=%.6f min_ms=%.6f event_TFLOPS=%.3f "
