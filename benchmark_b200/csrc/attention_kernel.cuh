@@ -6,46 +6,50 @@
 // attention.cu:176-183), Sq != Skv with bottom-right causal masking
 // (attention.cu:167-174), ragged tails, head_dim 64 or 128.
 //
-// One CTA owns two 128-row Q tiles of one (batch, head) and streams that head's
-// K/V tiles (128 keys each) once for both:
+// Persistent CTAs (one per SM) walk work items = (batch, q head, 128-row Q
+// tile).  Each item streams its head's K/V tiles (128 keys each).  Roles:
 //
-//   warps 0-3  softmax for Q tile 0 (one TMEM lane = one query row per thread)
-//   warps 4-7  softmax for Q tile 1
-//   warp  8    TMA producer (Q once, then the K and V rings) and TMEM allocator
-//   warp  9    tcgen05.mma issuer (one thread)
+//   warps 0-7   softmax: warp w owns 16 query rows (TMEM lanes
+//               32*(w%4) + 16*(w/4) + [0,16)), four threads per row
+//   warps 8-11  epilogue: O / l -> bf16 -> shared -> TMA store
+//   warp  12    TMA producer for Q (per item) and the K ring; TMEM allocator
+//   warp  13    tcgen05.mma issuer (whole warp, one elected lane issues)
+//   warp  14    TMA producer for the V ring (its own thread, so K loads run
+//               ahead of the V ring's slower turnover)
 //
-// All matrix products are M=128 x N=128 (S = Q K^T over 128 keys, O += P V over
-// 128 head dims, or 64 for D=64): issued back to back, that stream runs at the
-// full tensor rate on B200, while N=64 products run ~1.8x below theirs.
+// TMEM (512 columns): three S buffers [0,128) [128,256) [256,384) rotate over
+// the global tile sequence; O at [384, 384+D).  P (bf16 pairs) overwrites the
+// first 64 columns of its S buffer; keys 0-63 land in columns [0,32), keys
+// 64-127 in [32,64).  The epilogue of an item reads O while the softmax
+// already works on the next item; the next item's first PV waits for it.
 //
-// TMEM (512 columns):
-//   D=128: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512); P_i (bf16
-//          pairs, 64 columns) overwrites the first half of S_i.
-//   D=64:  S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384) P0 [384,448)
-//          P1 [448,512): P has its own columns.
-// PV reads P straight from TMEM (A operand in TMEM, V from shared memory,
-// MN-major).  P is produced in two 64-key halves with separate ready barriers,
-// so the first four PV MMAs run while the softmax computes the second half.
+// Why this shape: the tensor core runs M=128 products at full rate only for
+// N >= 128 with one operand in TMEM or both streams within the 128 B/clk
+// shared-memory read budget, and MUFU exp2 (16/clk/SM) costs as many cycles
+// per K/V tile as the two 128x128x128 products.  Three S buffers let S(t+1)
+// and S(t+2) run while the softmax of tile t runs, so neither the tensor core
+// nor the softmax waits on the other's latency and softmax warps may drift a
+// tile apart; eight independent softmax warps (16 rows each) put two on
+// every scheduler without any cross-warp barrier.
 //
-// MMA issue order per KV tile j:
-//   D=128: PV0(j) S0(j+1) PV1(j) S1(j+1)   (S_i(j+1) overwrites P_i(j); the
-//          tensor pipe executes one thread's MMAs in issue order)
-//   D=64:  S0(j+1) S1(j+1) PV0(j) PV1(j)   (S_i(j+1) is issued as soon as the
-//          softmax has read S_i(j) into registers; the softmax waits for
-//          PV_i(j) before writing P_i(j+1) or rescaling O_i)
-// The issuer polls every dependency of a step in one instruction group
-// (mbar_wait3): a barrier poll whose result is branched on costs a few hundred
-// cycles, and the tensor pipe queues only ~4 MMAs.
+// MMA issue order over the global tile stream t (crossing item boundaries):
+//   S(0), S(1), then for every t: S(t+2), PV(t)   (PV(t) in two 64-key
+//   halves, each issued when all eight softmax warps have stored that half
+//   of P(t)).  S(t+3) overwrites P(t) after PV(t) in issue order; the tensor
+//   pipe executes one thread's MMAs in issue order.
 //
-// Softmax: per row, running max m in log2 units; O and the row sum are
-// rescaled only when a block raises m by more than kRescaleLog2 (otherwise P
-// values up to 2^kRescaleLog2 accumulate unscaled: exact in fp32, and O / l is
-// unchanged).  exp2 runs on the MUFU for most elements and on the FMA pipe
-// (exp2_fma_x2, ptx.cuh) for kEmu of every 8 element pairs, so the two pipes
-// share the load; masked blocks use the MUFU only (exact zeros).
+// Softmax per tile: a thread reads 32 scores of each of its two rows
+// (16x256b TMEM loads), the row max is completed by two shuffles, and the
+// running max m is kept in log2 units.  O and the row sums are rescaled only
+// when a block raises m by more than kRescaleLog2 (otherwise P values up to
+// 2^kRescaleLog2 accumulate unscaled: exact in fp32, O / l unchanged), after
+// PV(t-1) has completed.  P is stored with 16x128b stores, whose column
+// order matches the key pairs each thread holds.
 //
-// Every wait is bounded (ptx.cuh); a timeout sets the device status word and
-// every role unwinds to the common teardown without trapping.
+// Every wait is bounded (ptx.cuh).  A timeout sets the device status word;
+// the epilogue warps, which meet at a named barrier, agree on aborting
+// through a shared flag written before the barrier, so no barrier is ever
+// left one-sided.
 #pragma once
 
 #include "ptx.cuh"
@@ -53,25 +57,30 @@
 namespace b200 {
 namespace attn {
 
-constexpr int kBM = 128;  // query rows per Q tile (= TMEM lanes)
+constexpr int kBM = 128;  // query rows per work item (= TMEM lanes)
 constexpr int kBN = 128;  // keys per K/V tile
-constexpr int kThreads = 320;
-constexpr int kTmaWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kEpiWarp0 = 8;
+constexpr int kTmaWarp = 12;   // Q and K loads
+constexpr int kMmaWarp = 13;
+constexpr int kTmaVWarp = 14;  // V loads
+constexpr int kThreads = 480;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kSBufs = 3;  // S buffers in TMEM (P overwrites its S buffer)
+constexpr int kBarEpilogue = 1;  // named barrier: warps 8-11
 
 struct Params {
   int B, Hq, Hkv, Sq, Skv;
-  int group;       // Hq / Hkv
-  int n_qpairs;    // ceil(Sq / 256)
+  int group;     // Hq / Hkv
+  int n_qtiles;  // ceil(Sq / 128)
+  int n_items;   // B * Hq * n_qtiles
   int causal;      // bottom-right aligned
   int causal_off;  // Skv - Sq
   float scale_log2;  // softmax_scale * log2(e)
   // Clock trace (kTrace instantiations only): per-role record regions of
   // trace_cap records (2 x u64: (event << 32 | tile << 24 | iter), clock64)
-  // for CTA trace_cta.  Role r (0 TMA, 1 MMA, 2/3 softmax tile 0/1) starts
-  // at trace + r * trace_cap * 2.
+  // for CTA trace_cta.  Role r (0 TMA, 1 MMA, 2/3 softmax keys 0-63/64-127,
+  // 4 epilogue) starts at trace + r * trace_cap * 2.
   unsigned long long* trace;
   int trace_cap;
   int trace_cta;
@@ -80,7 +89,8 @@ struct Params {
 // Clock-trace events (kTrace); names in benchmark_b200/trace.py.
 enum : uint32_t {
   kEvTmaK = 1, kEvTmaV, kEvMmaS, kEvMmaPvLo, kEvMmaPvHi, kEvSmWait, kEvSmReady, kEvSmLdDone,
-  kEvSmMaxDone, kEvSmPLo, kEvSmPHi, kEvEpiBegin, kEvEpiEnd, kEvMmaWait, kEvMmaEnd
+  kEvSmMaxDone, kEvSmPLo, kEvSmPHi, kEvEpiBegin, kEvEpiEnd, kEvMmaWait, kEvMmaEnd, kEvMmaGo,
+  kEvTmaQ
 };
 
 template <bool kTrace>
@@ -109,41 +119,38 @@ struct Tracer {
 template <int D>
 struct Cfg {
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
-  static constexpr bool kEarlyS = (D == 64);       // S(j+1) before PV(j), own P columns
   static constexpr int kBoxes = D / 64;            // 64-column (128-byte) TMA boxes per tile
   static constexpr int kBoxBytes = 128 * 128;      // 128 rows x 128 B = 16 KiB
   static constexpr int kTileBytes = kBoxes * kBoxBytes;
-  static constexpr int kStages = (D == 128) ? 2 : 4;  // K ring and V ring depth
-  static constexpr int kQOff = 0;
+  static constexpr int kKStages = (D == 128) ? 3 : 4;  // K ring depth
+  static constexpr int kVStages = (D == 128) ? 2 : 4;  // V ring depth
+  static constexpr int kQOff = 0;                       // Q0, Q1 (also O staging)
   static constexpr int kKOff = 2 * kTileBytes;
-  static constexpr int kVOff = kKOff + kStages * kTileBytes;
-  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
-  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_ready[2], p_lo[2],
-  // p_hi[2], o_final[2], s_free[2], pv_done[2], drain
-  static constexpr int kNumBars = 1 + 4 * kStages + 2 * 6 + 1;
+  static constexpr int kVOff = kKOff + kKStages * kTileBytes;
+  static constexpr int kLOff = kVOff + kVStages * kTileBytes;  // row sums [2 items][128]
+  static constexpr int kFlagOff = kLOff + 2 * 128 * 4;        // abort flag (epilogue)
+  static constexpr int kBarOff = kFlagOff + 16;
+  // q_full[2] q_empty[2] k_full[K] k_empty[K] v_full[V] v_empty[V]
+  // s_ready[3] p_lo[3] p_hi[3] pv_done o_full o_empty l_ready[2] drain done
+  static constexpr int kNumBars = 4 + 2 * kKStages + 2 * kVStages + 3 * kSBufs + 1 + 4 + 2;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kTmemSlotOff + 16 + 1024;  // + 1 KiB alignment slack
+  static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB of shared memory a CTA may use");
   static constexpr uint32_t kIdescS = idesc_bf16_f32(128, kBN, false, false);
   static constexpr uint32_t kIdescO = idesc_bf16_f32(128, D, false, true);
-  static constexpr uint32_t kColO = 256;
-  static constexpr uint32_t kColP = kEarlyS ? 256 + 2 * D : 0;  // D=128: P_i over S_i
+  static constexpr uint32_t kColO = 128 * kSBufs;
 };
 
 // Wait sites reported in the status word.
 enum : uint32_t {
   kSiteQFull = 1, kSiteKFull, kSiteVFull, kSitePReady, kSiteKEmpty, kSiteVEmpty,
-  kSiteSReady, kSiteOFinal, kSiteSFree, kSitePvDone
+  kSiteSReady, kSiteOFull, kSiteQEmpty, kSitePvDone, kSiteOEmpty, kSiteLReady
 };
 
-// Number of K/V tiles Q tile `tile_row0` must visit (0 if it has no rows or no
+// Number of K/V tiles the Q tile at `tile_row0` must visit (0 if it has no
 // valid keys) and the smallest per-row key limit inside the tile.
 __device__ __forceinline__ void tile_extent(const Params& p, int tile_row0, int* nblk,
                                             int* min_lim) {
-  if (tile_row0 >= p.Sq) {
-    *nblk = 0;
-    *min_lim = 0;
-    return;
-  }
   const int last_q = min(tile_row0 + kBM - 1, p.Sq - 1);
   int lim = p.Skv;
   int lim0 = p.Skv;
@@ -155,10 +162,48 @@ __device__ __forceinline__ void tile_extent(const Params& p, int tile_row0, int*
   *min_lim = lim0;
 }
 
-// Warp-uniform bounded wait for the softmax warps: the warp proceeds only if
-// every lane observed the phase (warp-collective tcgen05.ld/st never run on a
-// partial warp); waiting lanes sleep in the hardware wait so they do not take
-// issue slots from the MMA and TMA warps that share their schedulers.
+struct Item {
+  int zq;    // (b * Hq + hq): plane of Q / O
+  int zkv;   // (b * Hkv + hkv): plane of K / V
+  int row0;  // first query row
+  int n;     // K/V tiles to visit
+  int min_lim;
+};
+
+// Work item k.  Non-causal: items of one head are adjacent, so the CTAs
+// running at one time share a few heads' K/V in L2.  Causal: the heaviest Q
+// tiles (last rows) come first.
+__device__ __forceinline__ Item decode_item(const Params& p, int k) {
+  const int bhs = p.B * p.Hq;
+  int bh, qt;
+  if (p.causal) {
+    qt = p.n_qtiles - 1 - k / bhs;
+    bh = k - (k / bhs) * bhs;
+  } else {
+    bh = k / p.n_qtiles;
+    qt = k - bh * p.n_qtiles;
+  }
+  const int b = bh / p.Hq;
+  const int hq = bh - b * p.Hq;
+  Item it;
+  it.zq = bh;
+  it.zkv = b * p.Hkv + hq / p.group;
+  it.row0 = qt * kBM;
+  tile_extent(p, it.row0, &it.n, &it.min_lim);
+  return it;
+}
+
+// The r-th item of this CTA: rounds of gridDim.x items; causal rounds
+// alternate direction so every CTA gets a similar total of K/V tiles.
+__device__ __forceinline__ int item_index(const Params& p, int r) {
+  const int g = static_cast<int>(gridDim.x);
+  const int c = static_cast<int>(blockIdx.x);
+  return r * g + ((p.causal && (r & 1)) ? g - 1 - c : c);
+}
+
+// Warp-uniform bounded wait: true only if every lane observed the phase
+// (warp-collective tcgen05.ld/st never run on a partial warp).  Waiting lanes
+// sleep in the hardware wait so they do not take issue slots from others.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t site) {
   const bool ok = mbar_wait(bar, parity, site, kDefaultWaitLimitNs, 20000u);
   return __all_sync(0xffffffffu, ok);
@@ -174,27 +219,38 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// One 64-key half of P for this thread's row: exp2(x) as 32 bf16 pairs,
-// x = s * sc - m (s pre-scaled in masked blocks, sc = 1).  Accumulates the
-// fp32 row sum in packed pairs.
+// P for 32 keys of each of this thread's two rows (8 repeats of the
+// 16x256b layout: s[4g], s[4g+1] row a, s[4g+2], s[4g+3] row b): exp2(x) as
+// bf16 pairs, x = s * sc - m (s pre-scaled in masked blocks, sc = 1); pk[2g]
+// row a, pk[2g+1] row b (the 16x128b store order).  Accumulates fp32 row
+// sums in packed pairs.  kEmu of every 8 pairs use the FMA-pipe exp2
+// (exp2_fma_x2), the rest MUFU; masked blocks use MUFU only (exact zeros).
 template <int kEmu, bool kMasked>
-__device__ __forceinline__ void p_half(const float* s, float sc, float nm, uint64_t (&rs)[2],
-                                       uint32_t (&pk)[32]) {
+__device__ __forceinline__ void p_rows(const float* s, float sc, float nm_a, float nm_b,
+                                       uint64_t& rs_a, uint64_t& rs_b, uint32_t (&pk)[16]) {
   const uint64_t sc2 = f2_pack(sc, sc);
-  const uint64_t nm2 = f2_pack(nm, nm);
+  const uint64_t na2 = f2_pack(nm_a, nm_a);
+  const uint64_t nb2 = f2_pack(nm_b, nm_b);
 #pragma unroll
-  for (int e = 0; e < 32; ++e) {
-    const uint64_t x2 = f2_fma(f2_pack(s[2 * e], s[2 * e + 1]), sc2, nm2);
-    float x0, x1, p0, p1;
-    f2_unpack(x2, x0, x1);
-    if (!kMasked && (e & 7) < kEmu) {
-      exp2_fma_x2(x0, x1, p0, p1);
-    } else {
-      p0 = ex2_approx(x0);
-      p1 = ex2_approx(x1);
+  for (int g = 0; g < 8; ++g) {
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint64_t x2 = f2_fma(f2_pack(s[4 * g + 2 * rr], s[4 * g + 2 * rr + 1]), sc2,
+                                 rr ? nb2 : na2);
+      float x0, x1, p0, p1;
+      f2_unpack(x2, x0, x1);
+      if (!kMasked && ((2 * g + rr) & 7) < kEmu) {
+        exp2_fma_x2(x0, x1, p0, p1);
+      } else {
+        p0 = ex2_approx(x0);
+        p1 = ex2_approx(x1);
+      }
+      if (rr)
+        rs_b = f2_add(rs_b, f2_pack(p0, p1));
+      else
+        rs_a = f2_add(rs_a, f2_pack(p0, p1));
+      pk[2 * g + rr] = pack_bf16x2(p0, p1);
     }
-    rs[e & 1] = f2_add(rs[e & 1], f2_pack(p0, p1));
-    pk[e] = pack_bf16x2(p0, p1);
   }
 }
 
@@ -211,56 +267,57 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* q_buf = smem + C::kQOff;
   uint8_t* k_buf = smem + C::kKOff;
   uint8_t* v_buf = smem + C::kVOff;
+  float* lsum = reinterpret_cast<float*>(smem + C::kLOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kFlagOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + C::kStages;
-  uint64_t* v_full = k_empty + C::kStages;
-  uint64_t* v_empty = v_full + C::kStages;
-  uint64_t* s_ready = v_empty + C::kStages;
-  uint64_t* p_lo = s_ready + 2;
-  uint64_t* p_hi = p_lo + 2;
-  uint64_t* o_final = p_hi + 2;
-  uint64_t* s_free = o_final + 2;
-  uint64_t* pv_done = s_free + 2;
-  uint64_t* drain = pv_done + 2;
+  uint64_t* q_empty = q_full + 2;
+  uint64_t* k_full = q_empty + 2;
+  uint64_t* k_empty = k_full + C::kKStages;
+  uint64_t* v_full = k_empty + C::kKStages;
+  uint64_t* v_empty = v_full + C::kVStages;
+  uint64_t* s_ready = v_empty + C::kVStages;
+  uint64_t* p_lo = s_ready + kSBufs;
+  uint64_t* p_hi = p_lo + kSBufs;
+  uint64_t* pv_done = p_hi + kSBufs;
+  uint64_t* o_full = pv_done + 1;
+  uint64_t* o_empty = o_full + 1;
+  uint64_t* l_ready = o_empty + 1;
+  uint64_t* drain = l_ready + 2;
+  uint64_t* done = drain + 1;  // phase 0 completes at setup and never changes
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmemSlotOff);
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
-
-  // ---- work item: (batch, q head, pair of Q tiles) ----
-  int qpair = static_cast<int>(blockIdx.x % static_cast<uint32_t>(p.n_qpairs));
-  const int bh = static_cast<int>(blockIdx.x / static_cast<uint32_t>(p.n_qpairs));
-  if (p.causal) qpair = p.n_qpairs - 1 - qpair;  // heaviest tiles launch first
-  const int b = bh / p.Hq;
-  const int hq = bh - b * p.Hq;
-  const int zq = bh;                            // (b * Hq + hq) plane of Q / O
-  const int zkv = b * p.Hkv + hq / p.group;     // (b * Hkv + hkv) plane of K / V
-  const int row0[2] = {qpair * 2 * kBM, qpair * 2 * kBM + kBM};
-  int nblk[2], min_lim[2];
-  tile_extent(p, row0[0], &nblk[0], &min_lim[0]);
-  tile_extent(p, row0[1], &nblk[1], &min_lim[1]);
-  const int nmax = max(nblk[0], nblk[1]);
+  const int rounds = (p.n_items + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
 
   // ---- setup ----
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < C::kStages; ++s) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&l_ready[i], 8);
+    }
+    for (int i = 0; i < kSBufs; ++i) {
+      mbar_init(&s_ready[i], 1);
+      mbar_init(&p_lo[i], 8);
+      mbar_init(&p_hi[i], 8);
+    }
+    mbar_init(o_full, 1);
+    mbar_init(o_empty, 128);
+    for (int s = 0; s < C::kKStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < C::kVStages; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_ready[i], 1);
-      mbar_init(&p_lo[i], 128);
-      mbar_init(&p_hi[i], 128);
-      mbar_init(&o_final[i], 1);
-      mbar_init(&s_free[i], 128);
-      mbar_init(&pv_done[i], 1);
-    }
+    mbar_init(pv_done, 1);
     mbar_init(drain, 1);
+    mbar_init(done, 1);
+    mbar_arrive(done);
+    abort_flag[0] = 0;
     fence_mbar_init();
   }
   if (warp == kTmaWarp) {
@@ -279,357 +336,478 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const bool trace_cta = kTrace && static_cast<int>(blockIdx.x) == p.trace_cta;
 
-  if (warp == kTmaWarp) {
-    // ================= TMA producer =================
-    if (lane == 0 && nmax > 0) {
-      Tracer<kTrace> tr(p, 0, trace_cta);
+  if (warp == kTmaWarp || warp == kTmaVWarp) {
+    // ================= TMA producers (Q + K, and V) =================
+    if (lane == 0) {
+      const bool is_k = warp == kTmaWarp;
+      Tracer<kTrace> tr(p, 0, trace_cta && is_k);
       const uint64_t pol_q = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
-      uint32_t q_bytes = 0;
-      for (int i = 0; i < 2; ++i) q_bytes += nblk[i] > 0 ? C::kTileBytes : 0;
-      mbar_arrive_expect_tx(q_full, q_bytes);
-      for (int i = 0; i < 2; ++i) {
-        if (nblk[i] == 0) continue;
-        for (int h = 0; h < C::kBoxes; ++h)
-          tma_load_3d(q_buf + i * C::kTileBytes + h * C::kBoxBytes, &q_map, q_full, h * 64,
-                      row0[i], zq, pol_q);
-      }
-      int issued = 0;
+      int t = 0, li = 0, issued = 0, q_issued = -1;
       bool ok = true;
-      for (int j = 0; j < nmax && ok; ++j) {
-        const int s = j % C::kStages;
-        const uint32_t ph = static_cast<uint32_t>(j / C::kStages) & 1u;
-        ok = mbar_wait(&k_empty[s], ph ^ 1u, kSiteKEmpty);
-        if (!ok) break;
-        tr(kEvTmaK, 0, j);
-        mbar_arrive_expect_tx(&k_full[s], C::kTileBytes);
-        for (int h = 0; h < C::kBoxes; ++h)
-          tma_load_3d(k_buf + s * C::kTileBytes + h * C::kBoxBytes, &k_map, &k_full[s], h * 64,
-                      j * kBN, zkv, pol_kv);
-        ok = mbar_wait(&v_empty[s], ph ^ 1u, kSiteVEmpty);
-        if (!ok) {
-          issued = j;  // K(j) in flight, V(j) not
-          drain_wait(&k_full[s], ph);
-          break;
+      for (int r = 0; r < rounds && ok; ++r) {
+        const int k = item_index(p, r);
+        if (k >= p.n_items) continue;
+        const Item it = decode_item(p, k);
+        const int qb = li & 1;
+        const uint32_t qpar = static_cast<uint32_t>(li >> 1) & 1u;
+        ++li;
+        if (is_k) {
+          // Q(li) reuses the buffer the epilogue of item li-2 staged O in.
+          ok = mbar_wait(&q_empty[qb], qpar ^ 1u, kSiteQEmpty);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&q_full[qb], C::kTileBytes);
+          for (int h = 0; h < C::kBoxes; ++h)
+            tma_load_3d(q_buf + qb * C::kTileBytes + h * C::kBoxBytes, &q_map, &q_full[qb],
+                        h * 64, it.row0, it.zq, pol_q);
+          q_issued = li - 1;
+          tr(kEvTmaQ, qb, li - 1);
         }
-        tr(kEvTmaV, 0, j);
-        mbar_arrive_expect_tx(&v_full[s], C::kTileBytes);
-        for (int h = 0; h < C::kBoxes; ++h)
-          tma_load_3d(v_buf + s * C::kTileBytes + h * C::kBoxBytes, &v_map, &v_full[s], h * 64,
-                      j * kBN, zkv, pol_kv);
-        issued = j + 1;
+        for (int j = 0; j < it.n; ++j, ++t) {
+          if (is_k) {
+            const int ks = t % C::kKStages;
+            ok = mbar_wait(&k_empty[ks], (static_cast<uint32_t>(t / C::kKStages) & 1u) ^ 1u,
+                           kSiteKEmpty);
+            if (!ok) break;
+            tr(kEvTmaK, 0, t);
+            mbar_arrive_expect_tx(&k_full[ks], C::kTileBytes);
+            for (int h = 0; h < C::kBoxes; ++h)
+              tma_load_3d(k_buf + ks * C::kTileBytes + h * C::kBoxBytes, &k_map, &k_full[ks],
+                          h * 64, j * kBN, it.zkv, pol_kv);
+          } else {
+            const int vs = t % C::kVStages;
+            ok = mbar_wait(&v_empty[vs], (static_cast<uint32_t>(t / C::kVStages) & 1u) ^ 1u,
+                           kSiteVEmpty);
+            if (!ok) break;
+            mbar_arrive_expect_tx(&v_full[vs], C::kTileBytes);
+            for (int h = 0; h < C::kBoxes; ++h)
+              tma_load_3d(v_buf + vs * C::kTileBytes + h * C::kBoxBytes, &v_map, &v_full[vs],
+                          h * 64, j * kBN, it.zkv, pol_kv);
+          }
+          issued = t + 1;
+        }
       }
       if (!ok) {
         // Unwinding: let every copy already issued land before the CTA exits.
-        drain_wait(q_full, 0);
-        for (int j = max(0, issued - C::kStages); j < issued; ++j) {
-          const int s = j % C::kStages;
-          const uint32_t ph = static_cast<uint32_t>(j / C::kStages) & 1u;
-          drain_wait(&k_full[s], ph);
-          drain_wait(&v_full[s], ph);
+        if (is_k) {
+          if (q_issued >= 0)
+            drain_wait(&q_full[q_issued & 1], static_cast<uint32_t>(q_issued >> 1) & 1u);
+          for (int i = max(0, issued - C::kKStages); i < issued; ++i)
+            drain_wait(&k_full[i % C::kKStages], static_cast<uint32_t>(i / C::kKStages) & 1u);
+        } else {
+          for (int i = max(0, issued - C::kVStages); i < issued; ++i)
+            drain_wait(&v_full[i % C::kVStages], static_cast<uint32_t>(i / C::kVStages) & 1u);
         }
       }
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // ================= MMA issuer =================
-    if (lane == 0 && nmax > 0) {
-      Tracer<kTrace> tr(p, 1, trace_cta);
+    // The whole warp runs this loop (operands stay warp-uniform); one elected
+    // lane issues each MMA and commit.
+    {
+      Tracer<kTrace> tr(p, 1, trace_cta && lane == 0);
       const uint32_t q_addr = smem_u32(q_buf);
       const uint32_t k_addr = smem_u32(k_buf);
       const uint32_t v_addr = smem_u32(v_buf);
-      // q_full phase 0 completes once and stays complete: fills unused wait slots.
-      const uint32_t dn_a = smem_u32(q_full), dn_p = 0;
-      auto bar = [](uint64_t* b_) { return smem_u32(b_); };
-      auto par = [](int j) { return static_cast<uint32_t>(j) & 1u; };
-      auto kpar = [](int j) { return static_cast<uint32_t>(j / C::kStages) & 1u; };
-
-      // Descriptors are built once; a K step or ring stage only moves the
-      // start address, i.e. adds (byte offset >> 4) to the low field (shared
-      // addresses stay below 2^18, so the 14-bit field never carries).
+      // Descriptors are built once; a K step, ring stage or Q buffer only
+      // moves the start address, i.e. adds (byte offset >> 4) to the low
+      // field (shared addresses stay below 2^18: the 14-bit field never carries).
       const uint64_t dq0 = sdesc_sw128(q_addr, 16, 1024);
       const uint64_t dk0 = sdesc_sw128(k_addr, 16, 1024);
       const uint64_t dv0 = sdesc_sw128(v_addr, C::kBoxBytes, 1024);
       constexpr uint32_t kTile16 = C::kTileBytes >> 4, kBox16 = C::kBoxBytes >> 4;
-      const uint32_t tS[2] = {tmem_base, tmem_base + 128};
-      const uint32_t tO[2] = {tmem_base + C::kColO, tmem_base + C::kColO + D};
-      const uint32_t tP[2] = {C::kEarlyS ? tmem_base + C::kColP : tS[0],
-                              C::kEarlyS ? tmem_base + C::kColP + 64 : tS[1]};
-
-      auto issue_s = [&](int i, int j) {
-        tr(kEvMmaS, i, j);
-        const uint64_t dq = dq0 + i * kTile16;
-        const uint64_t dk = dk0 + (j % C::kStages) * kTile16;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kBox16 + (kk & 3) * 2;
-          mma_ss(tS[i], dq + off, dk + off, C::kIdescS, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(&s_ready[i]);
-      };
-      // PV for keys [64*half, 64*half + 64) of V tile j.
-      auto issue_pv_half = [&](int i, int j, int half) {
-        tr(half ? kEvMmaPvHi : kEvMmaPvLo, i, j);
-        const uint64_t dv = dv0 + (j % C::kStages) * kTile16;
-#pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-          const int kk = half * 4 + k4;
-          mma_ts(tO[i], tP[i] + kk * 8, dv + kk * (2048 >> 4), C::kIdescO,
-                 (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        if (half) {
-          if (C::kEarlyS) mma_commit(&pv_done[i]);
-          if (j == nblk[i] - 1) mma_commit(&o_final[i]);
-        }
-      };
+      const uint32_t tO = tmem_base + C::kColO;
+      // Filler for unused slots of the grouped waits.
+      const uint32_t dn_a = smem_u32(done), dn_p = 0;
+      auto bar = [](uint64_t* b_) { return smem_u32(b_); };
+      auto kpar = [](int t_) { return static_cast<uint32_t>(t_ / C::kKStages) & 1u; };
+      auto vpar = [](int t_) { return static_cast<uint32_t>(t_ / C::kVStages) & 1u; };
       auto wait3 = [&](uint32_t a0, uint32_t p0, uint32_t a1, uint32_t p1, uint32_t a2,
                        uint32_t p2, uint32_t site) -> bool {
         tr(kEvMmaWait, site, 0);
-        if (!mbar_wait3(a0, p0, a1, p1, a2, p2, site)) return false;
+        if (!__all_sync(0xffffffffu, mbar_wait3(a0, p0, a1, p1, a2, p2, site))) return false;
         tc_fence_after();
+        tr(kEvMmaGo, site, 0);
+        return true;
+      };
+      // S(t) = Q[qb] K(t)^T into S buffer t % kSBufs.
+      auto issue_s = [&](int t_, int qb) {
+        tr(kEvMmaS, qb, t_);
+        const uint64_t dq = dq0 + qb * kTile16;
+        const uint64_t dk = dk0 + (t_ % C::kKStages) * kTile16;
+        const uint32_t ts = tmem_base + static_cast<uint32_t>((t_ % kSBufs) * 128);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kBox16 + (kk & 3) * 2;
+          mma_ss_warp(ts, dq + off, dk + off, C::kIdescS, kk > 0 ? 1u : 0u);
+        }
+        mma_commit_warp(&k_empty[t_ % C::kKStages]);
+        mma_commit_warp(&s_ready[t_ % kSBufs]);
+      };
+      // O (+)= P(t)[keys 64*half ...] V(t)[keys 64*half ...]
+      auto issue_pv_half = [&](int t_, bool first, int half) {
+        tr(half ? kEvMmaPvHi : kEvMmaPvLo, 0, t_);
+        const uint64_t dv = dv0 + (t_ % C::kVStages) * kTile16;
+        const uint32_t tp = tmem_base + static_cast<uint32_t>((t_ % kSBufs) * 128);
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int kk = half * 4 + k4;
+          mma_ts_warp(tO, tp + kk * 8, dv + kk * (2048 >> 4), C::kIdescO,
+                      (!first || kk > 0) ? 1u : 0u);
+        }
+      };
+      // Next valid round after r (rounds if none).
+      auto next_round = [&](int r) {
+        for (++r; r < rounds; ++r)
+          if (item_index(p, r) < p.n_items) break;
+        return r;
+      };
+
+      // S cursor: the next S to issue, up to kSBufs - 1 tiles ahead of the
+      // PV cursor and never beyond the item after the PV cursor's (the Q of
+      // a later item waits for an epilogue that waits for this thread).
+      int s_r = next_round(-1), s_li = 0, s_j = 0, s_t = 0;
+      Item s_it{};
+      auto s_settle = [&]() {  // move past items without K/V tiles
+        while (s_r < rounds) {
+          s_it = decode_item(p, item_index(p, s_r));
+          if (s_it.n > 0) break;
+          s_r = next_round(s_r);
+          ++s_li;
+        }
+      };
+      s_settle();
+      auto issue_s_upto = [&](int limit_t, int max_li) -> bool {
+        while (s_r < rounds && s_t <= limit_t && s_li <= max_li) {
+          const int qb = s_li & 1;
+          if (s_j == 0 &&
+              !wait3(bar(&q_full[qb]), static_cast<uint32_t>(s_li >> 1) & 1u, dn_a, dn_p, dn_a,
+                     dn_p, kSiteQFull))
+            return false;
+          if (!wait3(bar(&k_full[s_t % C::kKStages]), kpar(s_t), dn_a, dn_p, dn_a, dn_p,
+                     kSiteKFull))
+            return false;
+          issue_s(s_t, qb);
+          ++s_t;
+          if (++s_j == s_it.n) {
+            s_j = 0;
+            s_r = next_round(s_r);
+            ++s_li;
+            s_settle();
+          }
+        }
         return true;
       };
 
-      // Prologue: S(0) for both tiles.
-      bool ok = wait3(bar(q_full), 0, bar(&k_full[0]), 0, dn_a, dn_p, kSiteKFull);
-      if (ok) {
-        for (int i = 0; i < 2; ++i)
-          if (nblk[i] > 0) issue_s(i, 0);
-        mma_commit(&k_empty[0]);
-      }
-      for (int j = 0; j < nmax && ok; ++j) {
-        const int s = j % C::kStages;
-        const int jn = j + 1;
-        const bool more = jn < nmax;
-        const uint32_t kn_a = more ? bar(&k_full[jn % C::kStages]) : dn_a;
-        const uint32_t kn_p = more ? kpar(jn) : dn_p;
-        if constexpr (C::kEarlyS) {
-          // S(j+1) for both tiles as soon as the softmax has S(j) in registers.
-          if (more) {
-            ok = wait3(kn_a, kn_p, jn < nblk[0] ? bar(&s_free[0]) : dn_a,
-                       jn < nblk[0] ? par(j) : dn_p, jn < nblk[1] ? bar(&s_free[1]) : dn_a,
-                       jn < nblk[1] ? par(j) : dn_p, kSiteSFree);
-            if (!ok) break;
-            for (int i = 0; i < 2; ++i)
-              if (jn < nblk[i]) issue_s(i, jn);
-            mma_commit(&k_empty[jn % C::kStages]);
-          }
-          for (int i = 0; i < 2 && ok; ++i) {
-            if (j >= nblk[i]) continue;
-            ok = wait3(bar(&v_full[s]), kpar(j), bar(&p_lo[i]), par(j), dn_a, dn_p,
-                       kSitePReady);
-            if (!ok) break;
-            issue_pv_half(i, j, 0);
-            ok = wait3(bar(&p_hi[i]), par(j), dn_a, dn_p, dn_a, dn_p, kSitePReady);
-            if (!ok) break;
-            issue_pv_half(i, j, 1);
-          }
+      // PV cursor.
+      int t = 0, li = 0;
+      bool ok = true;
+      for (int r = next_round(-1); r < rounds && ok; r = next_round(r), ++li) {
+        const Item it = decode_item(p, item_index(p, r));
+        const uint32_t oe_par = (static_cast<uint32_t>(li) & 1u) ^ 1u;  // epilogue of li-1
+        if (it.n == 0) {
+          // No K/V tiles: O stays unwritten (the epilogue stores zeros in Q's
+          // buffer, so Q(li) must have landed first).
+          ok = wait3(bar(&q_full[li & 1]), static_cast<uint32_t>(li >> 1) & 1u, bar(o_empty),
+                     oe_par, dn_a, dn_p, kSiteQFull);
           if (!ok) break;
-          mma_commit(&v_empty[s]);
-        } else {
-          for (int i = 0; i < 2 && ok; ++i) {
-            if (j < nblk[i]) {
-              ok = wait3(bar(&v_full[s]), kpar(j), bar(&p_lo[i]), par(j), dn_a, dn_p,
-                         kSitePReady);
-              if (!ok) break;
-              issue_pv_half(i, j, 0);
-              // S_i(j+1) needs K(j+1) and overwrites P_i(j): after PV_i(j).
-              ok = wait3(bar(&p_hi[i]), par(j), jn < nblk[i] ? kn_a : dn_a,
-                         jn < nblk[i] ? kn_p : dn_p, dn_a, dn_p, kSitePReady);
-              if (!ok) break;
-              issue_pv_half(i, j, 1);
-            }
-            if (jn < nblk[i]) issue_s(i, jn);
-          }
-          if (!ok) break;
-          mma_commit(&v_empty[s]);
-          if (more) mma_commit(&k_empty[jn % C::kStages]);
+          mma_commit_warp(o_full);
+          continue;
         }
+        for (int j = 0; j < it.n && ok; ++j) {
+          const int tt = t + j;
+          const uint32_t tpar = static_cast<uint32_t>(tt / kSBufs) & 1u;
+          ok = issue_s_upto(tt + kSBufs - 1, li + 1);
+          if (!ok) break;
+          if (j == 0) {
+            // O is free once the epilogue of item li-1 has read it.
+            ok = wait3(bar(o_empty), oe_par, dn_a, dn_p, dn_a, dn_p, kSiteOEmpty);
+            if (!ok) break;
+          }
+          ok = wait3(bar(&v_full[tt % C::kVStages]), vpar(tt), bar(&p_lo[tt % kSBufs]), tpar,
+                     dn_a, dn_p, kSitePReady);
+          if (!ok) break;
+          issue_pv_half(tt, j == 0, 0);
+          ok = wait3(bar(&p_hi[tt % kSBufs]), tpar, dn_a, dn_p, dn_a, dn_p, kSitePReady);
+          if (!ok) break;
+          issue_pv_half(tt, j == 0, 1);
+          mma_commit_warp(&v_empty[tt % C::kVStages]);
+          mma_commit_warp(pv_done);
+        }
+        if (!ok) break;
+        mma_commit_warp(o_full);
+        t += it.n;
       }
       // Every MMA issued above has completed once this commit lands.
-      mma_commit(drain);
+      mma_commit_warp(drain);
       drain_wait(drain, 0);
-      tr(kEvMmaEnd, 0, nmax);
+      tr(kEvMmaEnd, 0, t);
     }
     __syncwarp();
+  } else if (warp < static_cast<uint32_t>(kEpiWarp0)) {
+    // ================= softmax (warps 0-7) =================
+    // Warp w owns 16 rows: TMEM lanes 32*(w%4) + 16*(w/4) + [0,16).  Thread
+    // t of the warp holds rows t/4 and t/4+8 and, of every 8 keys, the pair
+    // 2*(t%4), 2*(t%4)+1 (16x256b loads); that pair is one packed P column
+    // (16x128b stores), and a row's max needs only two shuffles among the
+    // four threads that share it.
+    const uint32_t quad = warp & 3u;
+    const int rbase = static_cast<int>(quad * 32 + (warp >> 2) * 16);
+    const int t0 = static_cast<int>(lane & 3u);
+    const int ra = rbase + static_cast<int>(lane >> 2);  // rows of this thread
+    const int rb = ra + 8;
+    const uint32_t lane_addr = static_cast<uint32_t>(rbase) << 16;
+    const float c = p.scale_log2;
+    Tracer<kTrace> tr(p, 2 + static_cast<int>(warp >> 2), trace_cta && quad == 0 && lane == 0);
+    int t = 0, li = 0;
+    bool ok = true;
+#pragma unroll 1
+    for (int r = 0; r < rounds && ok; ++r) {
+      const int k = item_index(p, r);
+      if (k >= p.n_items) continue;
+      const Item it = decode_item(p, k);
+      const int qb = li & 1;
+      const uint32_t tO = tmem_base + lane_addr + C::kColO;
+      const int lim_a = p.causal ? min(p.Skv, it.row0 + ra + p.causal_off + 1) : p.Skv;
+      const int lim_b = p.causal ? min(p.Skv, it.row0 + rb + p.causal_off + 1) : p.Skv;
+      // Running max of scaled scores (log2 units) and this thread's share of
+      // the row sums, for rows a and b.
+      float m_a = -INFINITY, m_b = -INFINITY;
+      float l_a = 0.0f, l_b = 0.0f;
+      // S(tt) lives in sr once loaded; the load of a tile's successor is
+      // issued as soon as the tile's P is computed, so its latency overlaps
+      // the P stores and the bookkeeping.
+      uint32_t sr[64];
+      bool have_s = false;
+#pragma unroll 1
+      for (int j = 0; j < it.n; ++j) {
+        const int tt = t + j;
+        const int sb = tt % kSBufs;
+        const uint32_t tS = tmem_base + lane_addr + static_cast<uint32_t>(sb * 128);
+        tr(kEvSmWait, warp >> 2, tt);
+        if (!have_s) {
+          ok = warp_wait(&s_ready[sb], static_cast<uint32_t>(tt / kSBufs) & 1u, kSiteSReady);
+          if (!ok) break;
+          tc_fence_after();
+          tmem_ld_16x256b_x16(tS, sr);
+        }
+        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        have_s = false;
+        tr(kEvSmLdDone, warp >> 2, tt);
+        float* s = reinterpret_cast<float*>(sr);
+        const int kbase = j * kBN;
+        const bool masked = kbase + kBN > it.min_lim;  // uniform across the tile
+        float mx_a, mx_b;
+        if (masked) {
+          // Scale first, then mask, so masked keys are exactly -inf for any scale.
+          const int va = lim_a - kbase - 2 * t0, vb = lim_b - kbase - 2 * t0;
+          mx_a = -INFINITY;
+          mx_b = -INFINITY;
+#pragma unroll
+          for (int g = 0; g < 16; ++g) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float xa = 8 * g + e < va ? s[4 * g + e] * c : -INFINITY;
+              const float xb = 8 * g + e < vb ? s[4 * g + 2 + e] * c : -INFINITY;
+              s[4 * g + e] = xa;
+              s[4 * g + 2 + e] = xb;
+              mx_a = fmaxf(mx_a, xa);
+              mx_b = fmaxf(mx_b, xb);
+            }
+          }
+        } else {
+          // Four independent chains per row over the 16 repeats.
+          float a[4], b[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            a[u] = fmaxf(s[4 * u], s[4 * u + 1]);
+            b[u] = fmaxf(s[4 * u + 2], s[4 * u + 3]);
+          }
+#pragma unroll
+          for (int g = 4; g < 16; ++g) {
+            a[g & 3] = fmax3(a[g & 3], s[4 * g], s[4 * g + 1]);
+            b[g & 3] = fmax3(b[g & 3], s[4 * g + 2], s[4 * g + 3]);
+          }
+          mx_a = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])) * c;
+          mx_b = fmaxf(fmaxf(b[0], b[1]), fmaxf(b[2], b[3])) * c;
+        }
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+        tr(kEvSmMaxDone, warp >> 2, tt);
+
+        // Running-max update with lazy rescaling (per row; the four threads
+        // of a row hold the same values, so they decide alike).
+        float f_a = 1.0f, f_b = 1.0f;
+        bool rescale = false;
+        if (m_a == -INFINITY) {
+          m_a = mx_a;  // no probability mass accumulated yet for this row
+        } else if (mx_a > m_a + kRescaleLog2) {
+          f_a = ex2_approx(m_a - mx_a);
+          m_a = mx_a;
+          rescale = true;
+        }
+        if (m_b == -INFINITY) {
+          m_b = mx_b;
+        } else if (mx_b > m_b + kRescaleLog2) {
+          f_b = ex2_approx(m_b - mx_b);
+          m_b = mx_b;
+          rescale = true;
+        }
+        const float nm_a = (m_a == -INFINITY) ? 0.0f : -m_a;
+        const float nm_b = (m_b == -INFINITY) ? 0.0f : -m_b;
+        const float sc = masked ? 1.0f : c;  // masked scores are pre-scaled
+        uint64_t rs_a = 0ull, rs_b = 0ull;
+        // P for keys 0-63 (repeats g = 0..7), then 64-127 (g = 8..15).
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[16];
+          if (masked)
+            p_rows<kEmu, true>(s + 32 * half, sc, nm_a, nm_b, rs_a, rs_b, pk);
+          else
+            p_rows<kEmu, false>(s + 32 * half, sc, nm_a, nm_b, rs_a, rs_b, pk);
+          tmem_st_16x128b_x8(tS + 32 * half, pk);
+        }
+        // S(tt+1), if it is this item's and already computed: start its load.
+        if (j + 1 < it.n) {
+          const int nb = (tt + 1) % kSBufs;
+          const bool ready = mbar_try_wait(smem_u32(&s_ready[nb]),
+                                           static_cast<uint32_t>((tt + 1) / kSBufs) & 1u);
+          have_s = __all_sync(0xffffffffu, ready);
+          if (have_s) {
+            tc_fence_after();
+            tmem_ld_16x256b_x16(tmem_base + lane_addr + static_cast<uint32_t>(nb * 128), sr);
+          }
+        }
+        if (__any_sync(0xffffffffu, rescale) && j > 0) {
+          // Rare: rescale the O rows whose maximum jumped, once PV(tt-1) has
+          // completed; PV(tt) waits for the P barriers below.
+          if (!warp_wait(pv_done, static_cast<uint32_t>(tt - 1) & 1u, kSitePvDone)) {
+            ok = false;
+          } else {
+            tc_fence_after();
+#pragma unroll 1
+            for (int c0 = 0; c0 < D; c0 += 64) {
+              uint32_t o[32];
+              tmem_ld_16x256b_x8(tO + c0, o);
+              tmem_wait_ld(o);
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                o[4 * g + 0] = __float_as_uint(__uint_as_float(o[4 * g + 0]) * f_a);
+                o[4 * g + 1] = __float_as_uint(__uint_as_float(o[4 * g + 1]) * f_a);
+                o[4 * g + 2] = __float_as_uint(__uint_as_float(o[4 * g + 2]) * f_b);
+                o[4 * g + 3] = __float_as_uint(__uint_as_float(o[4 * g + 3]) * f_b);
+              }
+              tmem_st_16x256b_x8(tO + c0, o);
+            }
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&p_lo[sb]);
+          mbar_arrive(&p_hi[sb]);
+        }
+        tr(kEvSmPLo, warp >> 2, tt);
+        float r0, r1;
+        f2_unpack(rs_a, r0, r1);
+        l_a = l_a * f_a + (r0 + r1);
+        f2_unpack(rs_b, r0, r1);
+        l_b = l_b * f_b + (r0 + r1);
+        if (!ok) break;
+      }
+      if (have_s) {
+        // Abandoned prefetch (only after an abort): let the load land.
+        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      }
+      if (!ok) break;
+      // Row sums over the four threads of each row, handed to the epilogue
+      // once it has finished the previous item (li - 1) and read its sums.
+      l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+      l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+      l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+      l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+      ok = warp_wait(o_empty, (static_cast<uint32_t>(li) & 1u) ^ 1u, kSiteOEmpty);
+      if (!ok) break;
+      if (t0 == 0) {
+        lsum[qb * 128 + ra] = l_a;
+        lsum[qb * 128 + rb] = l_b;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&l_ready[qb]);
+      t += it.n;
+      ++li;
+    }
   } else {
-    // ================= softmax + epilogue (warps 0-7) =================
-    const int i = static_cast<int>(warp >> 2);  // Q tile
+    // ================= epilogue (warps 8-11) =================
     const uint32_t quad = warp & 3u;
     const int row = static_cast<int>(quad * 32 + lane);
     const uint32_t lane_addr = (quad * 32u) << 16;
-    const uint32_t tS = tmem_base + lane_addr + static_cast<uint32_t>(i) * 128u;
-    const uint32_t tO = tmem_base + lane_addr + C::kColO + static_cast<uint32_t>(i * D);
-    const uint32_t tP =
-        C::kEarlyS ? tmem_base + lane_addr + C::kColP + static_cast<uint32_t>(i) * 64u : tS;
-    const int n = nblk[i];
-    const int q = row0[i] + row;
-    const int lim = p.causal ? min(p.Skv, q + p.causal_off + 1) : p.Skv;
-    const float c = p.scale_log2;
-    float m = -INFINITY;  // running max of scaled scores (log2 units)
-    float l = 0.0f;       // running row sum of P
-    bool ok = true;
-    Tracer<kTrace> tr(p, 2 + i, trace_cta && quad == 0 && lane == 0);
-
+    Tracer<kTrace> tr(p, 4, trace_cta && quad == 0 && lane == 0);
+    int li = 0;
 #pragma unroll 1
-    for (int j = 0; j < n; ++j) {
-      tr(kEvSmWait, i, j);
-      ok = warp_wait(&s_ready[i], static_cast<uint32_t>(j) & 1u, kSiteSReady);
-      if (!ok) break;
+    for (int r = 0; r < rounds; ++r) {
+      const int k = item_index(p, r);
+      if (k >= p.n_items) continue;
+      const Item it = decode_item(p, k);
+      const int qb = li & 1;
+      const uint32_t qpar = static_cast<uint32_t>(li >> 1) & 1u;
+      ++li;
+      tr(kEvEpiBegin, qb, li - 1);
+      const bool got =
+          warp_wait(o_full, static_cast<uint32_t>(li - 1) & 1u, kSiteOFull) &&
+          warp_wait(&l_ready[qb], qpar, kSiteLReady);
+      if (!got) abort_flag[0] = 1;
       tc_fence_after();
-      tr(kEvSmReady, i, j);
-      uint32_t sr[128];
-      tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-      tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
-      tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
-      tmem_wait_ld();
-      tr(kEvSmLdDone, i, j);
-      if constexpr (C::kEarlyS) {
-        // S_i is in registers: the MMA warp may overwrite it with S_i(j+1).
-        tc_fence_before();
-        mbar_arrive(&s_free[i]);
-      }
-      float* s = reinterpret_cast<float*>(sr);
-
-      const int kbase = j * kBN;
-      const bool masked = kbase + kBN > min_lim[i];  // uniform across the tile
-      float m_blk;
-      if (masked) {
-        // Scale first, then mask, so masked keys are exactly -inf for any scale.
-        const int valid = lim - kbase;
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int e = 0; e < kBN; ++e) {
-          const float t = e < valid ? s[e] * c : -INFINITY;
-          s[e] = t;
-          mx[e & 3] = fmaxf(mx[e & 3], t);
-        }
-        m_blk = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      } else {
-        // 3-input max: 4 independent chains over 124 values + 4 seeds.
-        float mx[4] = {s[0], s[1], s[2], s[3]};
-#pragma unroll
-        for (int e = 4; e < 124; e += 8) {
-          mx[0] = fmax3(mx[0], s[e + 0], s[e + 1]);
-          mx[1] = fmax3(mx[1], s[e + 2], s[e + 3]);
-          mx[2] = fmax3(mx[2], s[e + 4], s[e + 5]);
-          mx[3] = fmax3(mx[3], s[e + 6], s[e + 7]);
-        }
-        mx[0] = fmax3(mx[0], s[124], s[125]);
-        mx[1] = fmax3(mx[1], s[126], s[127]);
-        m_blk = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c;
-      }
-      tr(kEvSmMaxDone, i, j);
-
-      // Running-max update with lazy rescaling.
-      float factor = 1.0f;
-      bool rescale = false;
-      if (m == -INFINITY) {
-        m = m_blk;  // no probability mass accumulated yet for this row
-      } else if (m_blk > m + kRescaleLog2) {
-        factor = ex2_approx(m - m_blk);
-        m = m_blk;
-        rescale = true;
-      }
-      if constexpr (C::kEarlyS) {
-        // P_i and O_i are still in use by PV_i(j-1) until it completes.
-        if (j > 0) {
-          ok = warp_wait(&pv_done[i], static_cast<uint32_t>(j - 1) & 1u, kSitePvDone);
-          if (!ok) break;
-          tc_fence_after();
-        }
-      }
-
-      const float m_use = (m == -INFINITY) ? 0.0f : m;
-      const float sc = masked ? 1.0f : c;  // masked scores are pre-scaled
-      uint64_t rs[2] = {0ull, 0ull};
-      {
-        uint32_t pk[32];
-        if (masked)
-          p_half<kEmu, true>(s, sc, -m_use, rs, pk);
-        else
-          p_half<kEmu, false>(s, sc, -m_use, rs, pk);
-        tmem_st32(tP, pk);
-      }
-      // Rare: rescale the O rows whose maximum jumped.  PV_i(j-1) has
-      // completed (D=128: its commit preceded S_i(j)'s; D=64: waited above)
-      // and PV_i(j) waits for the P barriers below.
-      if (__any_sync(0xffffffffu, rescale) && j > 0) {
+      const uint32_t tO = tmem_base + lane_addr + C::kColO;
+      const float l = lsum[qb * 128 + row];
+      const bool have_o = got && it.n > 0;
+      const float inv = (have_o && l > 0.0f) ? 1.0f / l : 0.0f;
+      uint8_t* obuf = q_buf + qb * C::kTileBytes;
+      const uint32_t obase = smem_u32(obuf);
 #pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += 32) {
-          uint32_t o[32];
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
+        if (have_o) {
           tmem_ld32(tO + c0, o);
-          tmem_wait_ld();
+          tmem_wait_ld(o);
+        } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
-          tmem_st32(tO + c0, o);
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          w[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+        const int box = c0 >> 6;
+        const int chunk0 = (c0 & 63) >> 3;  // 16-byte chunk index inside the 128-byte row
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int ch = (chunk0 + u) ^ (row & 7);
+          st_shared_v4(obase + box * C::kBoxBytes + row * 128 + ch * 16, w[4 * u], w[4 * u + 1],
+                       w[4 * u + 2], w[4 * u + 3]);
         }
       }
-      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_lo[i]);
-      tr(kEvSmPLo, i, j);
-      {
-        uint32_t pk[32];
-        if (masked)
-          p_half<kEmu, true>(s + 64, sc, -m_use, rs, pk);
-        else
-          p_half<kEmu, false>(s + 64, sc, -m_use, rs, pk);
-        tmem_st32(tP + 32, pk);
+      mbar_arrive(o_empty);
+      fence_proxy_async_smem();
+      named_bar_sync(kBarEpilogue, 128);
+      if (abort_flag[0] != 0) break;
+      if (quad == 0 && lane == 0) {
+        for (int b = 0; b < C::kBoxes; ++b)
+          tma_store_3d(&o_map, obuf + b * C::kBoxBytes, b * 64, it.row0, it.zq);
+        bulk_commit_group();
+        bulk_wait_group_read<0>();
+        mbar_arrive(&q_empty[qb]);
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_hi[i]);
-      tr(kEvSmPHi, i, j);
-      float r0, r1, r2, r3;
-      f2_unpack(rs[0], r0, r1);
-      f2_unpack(rs[1], r2, r3);
-      l = l * factor + ((r0 + r1) + (r2 + r3));
+      tr(kEvEpiEnd, qb, li - 1);
+      __syncwarp();
     }
-
-    // ---- epilogue: O / l -> bf16 -> swizzled smem (reusing Q_i) -> TMA store ----
-    tr(kEvEpiBegin, i, n);
-    if (ok && n > 0) {
-      ok = warp_wait(&o_final[i], 0, kSiteOFinal);
-      tc_fence_after();
-    }
-    uint8_t* obuf = q_buf + i * C::kTileBytes;
-    const uint32_t obase = smem_u32(obuf);
-    const float inv = (ok && n > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
-#pragma unroll
-    for (int c0 = 0; c0 < D; c0 += 32) {
-      uint32_t o[32];
-      if (ok && n > 0) {
-        tmem_ld32(tO + c0, o);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = 0u;
-      }
-      uint32_t w[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e)
-        w[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
-      const int box = c0 >> 6;
-      const int chunk0 = (c0 & 63) >> 3;  // 16-byte chunk index inside the 128-byte row
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int ch = (chunk0 + t) ^ (row & 7);
-        st_shared_v4(obase + box * C::kBoxBytes + row * 128 + ch * 16, w[4 * t], w[4 * t + 1],
-                     w[4 * t + 2], w[4 * t + 3]);
-      }
-    }
-    fence_proxy_async_smem();
-    named_bar_sync(1 + i, 128);
-    if (quad == 0 && lane == 0 && row0[i] < p.Sq) {
-      for (int h = 0; h < C::kBoxes; ++h)
-        tma_store_3d(&o_map, obuf + h * C::kBoxBytes, h * 64, row0[i], zq);
-      bulk_commit_group();
-      bulk_wait_group_read<0>();
-    }
-    tr(kEvEpiEnd, i, n);
-    __syncwarp();
   }
 
   // ---- teardown ----

@@ -117,6 +117,13 @@ b200_status ensure_smem_attr(Kernel kernel, int bytes, unsigned* done_mask) {
   return B200_OK;
 }
 
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return n > 0 ? n : 148;
+}
+
 struct AttnShape {
   int B, Hq, Hkv, Sq, Skv, D, causal;
   float scale;
@@ -148,8 +155,10 @@ b200_status check_attention_args(const void* q, const void* k, const void* v, co
 
 // FMA-pipe exp2 share (pairs of every 8) per head_dim; B200_ATTN_EXP2_EMU
 // overrides it for tuning sweeps (values without an instantiation are rejected).
-constexpr int kDefaultEmuD128 = 0;
-constexpr int kDefaultEmuD64 = 0;
+// Measured on B200 (c2: d128, c4: d64 workloads): one pair in eight on the
+// FMA pipe for d128, two for d64, where MUFU is the tighter pipe.
+constexpr int kDefaultEmuD128 = 1;
+constexpr int kDefaultEmuD64 = 2;
 
 int exp2_emu_setting(int D) {
   static const int env_value = [] {
@@ -192,17 +201,19 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   p.Sq = s.Sq;
   p.Skv = s.Skv;
   p.group = s.Hq / s.Hkv;
-  p.n_qpairs = (s.Sq + 2 * b200::attn::kBM - 1) / (2 * b200::attn::kBM);
+  p.n_qtiles = (s.Sq + b200::attn::kBM - 1) / b200::attn::kBM;
+  const long long items = static_cast<long long>(pq) * p.n_qtiles;
+  if (items > 0x3fffffffll) return fail(B200_EUNSUPPORTED, "attention: too many work items");
+  p.n_items = static_cast<int>(items);
   p.causal = s.causal;
   p.causal_off = s.Skv - s.Sq;
   p.scale_log2 = s.scale * 1.4426950408889634f;
   p.trace = tr.buf;
   p.trace_cap = tr.cap;
   p.trace_cta = tr.cta;
-  const long long grid = static_cast<long long>(pq) * p.n_qpairs;
-  if (grid > 0x7fffffffll) return fail(B200_EUNSUPPORTED, "attention: grid too large");
-  kernel<<<static_cast<unsigned>(grid), b200::attn::kThreads, C::kSmemBytes, stream>>>(qm, km,
-                                                                                      vm, om, p);
+  // Persistent: one CTA per SM (shared memory admits one), or fewer items.
+  const int grid = static_cast<int>(std::min<long long>(items, sm_count()));
+  kernel<<<grid, b200::attn::kThreads, C::kSmemBytes, stream>>>(qm, km, vm, om, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "attention_fwd launch");
   return B200_OK;
@@ -235,12 +246,6 @@ b200_status check_gemm_args(const void* A, const void* Bm, const void* C, int M,
   return B200_OK;
 }
 
-int sm_count() {
-  int dev = 0, n = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
-  return n > 0 ? n : 148;
-}
 
 // One cuBLAS handle per (thread, device) for the comparator.
 cublasHandle_t cublas_handle(b200_status* st) {

@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c0 = 0; c0 < kBN; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(a * kBN + c0), v);
-        tmem_wait_ld();
+        tmem_wait_ld(v);
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e)
@@ -437,7 +437,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
       for (int c0 = 0; c0 < kBN; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(a * kBN + c0), v);
-        tmem_wait_ld();
+        tmem_wait_ld(v);
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e)
