@@ -36,6 +36,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "attention fwd TFLOPS per GPU and per box at 1/2/4/8 B200; % of bf16 tensor peak"
+GEMM_METRIC = "bf16 GEMM TFLOP/s (tcgen05 vs cuBLAS) at 8192^3"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # Per-GPU workloads.  "b" is the per-GPU batch.
@@ -49,6 +50,10 @@ WORKLOADS = {
     # config 4: B=64 sharded by batch over 8 GPUs: 8 per GPU.
     "c4": dict(name="attn_b64_h16_n2048_d64_per_gpu_b8", b=8, h=16, n=2048, d=64, causal=False,
                sigma=0.5),
+    # The GEMM path (5.GEMM): 8192^3, A and B ~ U(-1,1), B stored [K, N] as
+    # the reference stores it; each rank multiplies its own pair (weak scaling).
+    "gemm": dict(name="gemm_bf16_m8192_n8192_k8192_b_row_major", kind="gemm", m=8192, n=8192,
+                 k=8192),
 }
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel,
@@ -187,6 +192,22 @@ def cpu_reference_sample(w: dict, rows_per_thread: int, threads: int) -> dict:
     return {"seconds": dt, "flops": flops, "kind": "reference" if use_ref else "port"}
 
 
+def gemm_cpu_sample(w: dict, rows_per_thread: int, threads: int) -> dict:
+    """The oracle's double-precision GEMM loop (the reference's fp32 GEMM
+    algorithm, 5.GEMM/gemm256_tma_tcgen05_bench.cu:1115-1137, restated; the
+    reference has no CPU GEMM of its own) on rows_per_thread rows of C per
+    thread, full N and K."""
+    import oracle
+    rng = np.random.default_rng(7)
+    rows = rows_per_thread * threads
+    a = oracle.f32_to_bf16(rng.uniform(-1.0, 1.0, (rows, w["k"])).astype(np.float32))
+    b = oracle.f32_to_bf16(rng.uniform(-1.0, 1.0, (w["k"], w["n"])).astype(np.float32))
+    t0 = time.perf_counter()
+    oracle.gemm(a, b, False, 0, rows, threads=threads)
+    dt = time.perf_counter() - t0
+    return {"seconds": dt, "flops": 2.0 * rows * w["n"] * w["k"], "kind": "port"}
+
+
 def host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -199,25 +220,33 @@ def run_reference_arm(args, w: dict) -> None:
     if rank != 0:
         return
     threads = host_threads()
-    rows = args.cpu_rows
+    gemm = w.get("kind") == "gemm"
+    rows = args.cpu_gemm_rows if gemm else args.cpu_rows
+    sample_fn = gemm_cpu_sample if gemm else cpu_reference_sample
     for _ in range(args.warmup):
-        cpu_reference_sample(w, max(1, rows // 8), threads)
+        sample_fn(w, max(1, rows // 8), threads)
     times, flops, kind = [], 0.0, "port"
     for _ in range(args.steps):
-        r = cpu_reference_sample(w, rows, threads)
+        r = sample_fn(w, rows, threads)
         times.append(r["seconds"])
         flops, kind = r["flops"], r["kind"]
     t = sum(times) / len(times)
     value = flops / t / 1e12
-    sample = (f"{threads} threads x {rows} query rows x {w['n']} keys x d{w['d']}"
-              f"{' causal' if w['causal'] else ''} per step (1 head of K/V each)")
+    if gemm:
+        sample = (f"{threads} threads x {rows} rows of C x N={w['n']} x K={w['k']} per step")
+        config = {"workload": w["name"], "M": w["m"], "N": w["n"], "K": w["k"], "sampled": True}
+    else:
+        sample = (f"{threads} threads x {rows} query rows x {w['n']} keys x d{w['d']}"
+                  f"{' causal' if w['causal'] else ''} per step (1 head of K/V each)")
+        config = {"workload": w["name"], "B": w["b"], "H": w["h"], "N": w["n"], "D": w["d"],
+                  "causal": w["causal"], "sampled": True}
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "impl": "reference", "metric": GEMM_METRIC if gemm else METRIC, "value": value,
+        "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,sigma) bf16 inputs",
-        "config": {"workload": w["name"], "B": w["b"], "H": w["h"], "N": w["n"], "D": w["d"],
-                   "causal": w["causal"], "sampled": True},
+        "vs_baseline": None, "dtype": "f64" if gemm else "f32",
+        "data": "synthetic U(-1,1) bf16 inputs" if gemm else "synthetic N(0,sigma) bf16 inputs",
+        "config": config,
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -226,49 +255,197 @@ def run_reference_arm(args, w: dict) -> None:
 
 
 # ---------------------------------------------------------------------------
-# GPU arm
+# Rank plumbing shared by both arms (tested on CPU with gloo ranks)
 # ---------------------------------------------------------------------------
-def run_e2e(args, w, q, k, v, o, stream, world, dev, barrier, flops) -> dict:
-    """Same metric through the C-ABI call with host buffers: every step copies
-    Q/K/V from pinned host memory, runs the kernel and copies O back."""
+def rank_index_base(rank: int, elems_per_rank: int) -> int:
+    """First global element index of this rank's batch slice: rank r owns
+    batches [r*B, (r+1)*B) of the global [B*world, H, N, D] tensors, so its
+    generated values are those of that slice of one global tensor."""
+    return rank * elems_per_rank
+
+
+def max_over_ranks(value: float, world: int, device=None) -> float:
+    """The slowest rank's time: all ranks call this collectively."""
+    if world <= 1:
+        return float(value)
     import torch
     import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def pipelined_e2e(args, inputs, out, compute, stream, world, dev, barrier, flops) -> dict:
+    """The metric through the C-ABI call with host buffers: every step copies
+    the inputs from pinned host memory, runs `compute(device_inputs,
+    device_out)` on `stream` and copies the result back.  Steps are pipelined
+    over two device buffer sets on three streams (host->device, compute,
+    device->host), as a streaming caller would run them; the timed region
+    spans from the first copy in to the last copy out."""
+    import torch
 
     from benchmark_b200 import ops
 
-    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-    ho = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
-    dq, dk, dv, do = (torch.empty_like(q) for _ in range(4))
+    hosts = [t.cpu().pin_memory() for t in inputs]
+    h_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    bufs = [([torch.empty_like(t) for t in inputs], torch.empty_like(out)) for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev = lambda: torch.cuda.Event(enable_timing=False)  # noqa: E731
+    computed = [ev(), ev()]
+    drained = [ev(), ev()]
 
-    def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        ops.attention_fwd(dq, dk, dv, out=do, causal=w["causal"], stream=stream)
-        ho.copy_(do, non_blocking=True)
+    def e2e_step(i: int) -> None:
+        d_in, d_out = bufs[i & 1]
+        loaded = ev()
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(computed[i & 1])  # step i-2 has consumed this set
+            for d, h in zip(d_in, hosts):
+                d.copy_(h, non_blocking=True)
+            loaded.record(s_in)
+        stream.wait_event(loaded)
+        stream.wait_event(drained[i & 1])  # the result of step i-2 has been copied out
+        compute(d_in, d_out)
+        computed[i & 1].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(computed[i & 1])
+            h_out.copy_(d_out, non_blocking=True)
+            drained[i & 1].record(s_out)
 
-    steps = max(1, min(args.steps, args.e2e_steps))
-    for _ in range(2):
-        e2e_step()
+    steps = max(2, min(args.steps, args.e2e_steps))
+    for i in range(2):
+        e2e_step(i)
     torch.cuda.synchronize()
     barrier()
-    s = torch.cuda.Event(enable_timing=True)
-    e = torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    for _ in range(steps):
-        e2e_step()
-    e.record(stream)
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record(s_in)
+    for i in range(steps):
+        e2e_step(i)
+    s_in.wait_stream(s_out)
+    stop.record(s_in)
     torch.cuda.synchronize()
     ops.check(stream)
-    ms = torch.tensor([s.elapsed_time(e) / steps], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    if not torch.equal(ho, o.cpu()):
+    ms = max_over_ranks(start.elapsed_time(stop) / steps, world, dev)
+    if not torch.equal(h_out, out.cpu()):
         raise RuntimeError("e2e output differs from the device-resident run")
-    return {"value": world * flops / (float(ms.item()) * 1e-3) / 1e12, "unit": "TFLOP/s",
-            "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
-            "d2h_bytes_per_step": o.numel() * o.element_size(), "steps": steps,
-            "ms_per_step": float(ms.item())}
+    return {"value": world * flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in inputs),
+            "d2h_bytes_per_step": out.numel() * out.element_size(), "steps": steps,
+            "ms_per_step": ms, "pipelined": "2 buffer sets, H2D / compute / D2H streams"}
+
+
+def run_e2e(args, w, q, k, v, o, stream, world, dev, barrier, flops) -> dict:
+    from benchmark_b200 import ops
+
+    def compute(d_in, d_out):
+        ops.attention_fwd(d_in[0], d_in[1], d_in[2], out=d_out, causal=w["causal"],
+                          stream=stream)
+
+    return pipelined_e2e(args, [q, k, v], o, compute, stream, world, dev, barrier, flops)
+
+
+def run_gemm_arm(args, w: dict) -> None:
+    """The GEMM path: this library's tcgen05 CTA-pair kernel on C = A @ B with
+    B stored [K, N], every rank on its own operands; cuBLAS on the same
+    operands is reported beside it."""
+    import torch
+    import torch.distributed as dist
+
+    from benchmark_b200 import _lib, ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    M, N, K = w["m"], w["n"], w["k"]
+    a = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
+    b = torch.empty((K, N), dtype=torch.bfloat16, device=dev)
+    c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    ops.fill_uniform_(a, args.seed, 10, -1.0, 1.0, index_base=rank_index_base(rank, a.numel()))
+    ops.fill_uniform_(b, args.seed, 11, -1.0, 1.0, index_base=rank_index_base(rank, b.numel()))
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    flops = 2.0 * M * N * K
+
+    def timed(impl: str) -> float:
+        for _ in range(args.warmup):
+            ops.gemm_bf16(a, b, out=c, b_col_major=False, impl=impl, stream=stream)
+        ops.check(stream)
+        barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        stop = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            ops.gemm_bf16(a, b, out=c, b_col_major=False, impl=impl, stream=stream)
+        stop.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ops.check(stream)
+        return start.elapsed_time(stop) / args.steps
+
+    ms_cublas = max_over_ranks(timed("cublas"), world, dev)
+    with ClockSampler(local) as clocks:
+        ms_local = timed("tcgen05")
+    ms_max = max_over_ranks(ms_local, world, dev)
+    value = world * flops / (ms_max * 1e-3) / 1e12
+
+    def compute(d_in, d_out):
+        ops.gemm_bf16(d_in[0], d_in[1], out=d_out, b_col_major=False, stream=stream)
+
+    e2e = None if args.no_e2e else pipelined_e2e(args, [a, b], c, compute, stream, world, dev,
+                                                 barrier, flops)
+    peaks, peak_src = load_peaks()
+    peak = float(peaks["bf16_tflops"])
+    achieved = flops / (ms_local * 1e-3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
+        r = gemm_cpu_sample(w, args.cpu_gemm_rows, threads)
+        cpu = {"value": r["flops"] / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": threads,
+               "kind": r["kind"],
+               "sample": (f"{threads} threads x {args.cpu_gemm_rows} rows of C x N={N} x K={K} "
+                          f"({r['seconds']:.1f} s wall)")}
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": GEMM_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": f"synthetic: bf16 A, B ~ U(-1,1), counter-based seed {args.seed}",
+        "config": {"workload": w["name"], "M": M, "N": N, "K": K, "b_layout": "[K,N]",
+                   "parallelism": f"dp{world} (independent GEMM per rank)",
+                   "l2": "inputs larger than L2 (256 MiB of A and B per step)"},
+        "cublas_tflops": world * flops / (ms_cublas * 1e-3) / 1e12,
+        "vs_cublas": ms_cublas / ms_max,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES.get(args.workload),
+                     "algorithmic_bytes": 2 * (M * K + K * N + M * N),
+                     "kernel": "gemm_bf16_pair_kernel",
+                     "peak_source": f"{peak_src} bf16_tflops (burst)"},
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+        "lib": _lib.LIB_PATH.name,
+    }
+    print(json.dumps(line), flush=True)
 
 
 def run_gpu_arm(args, w: dict) -> None:
@@ -299,7 +476,8 @@ def run_gpu_arm(args, w: dict) -> None:
     per = q.numel()
     # this rank's batch slice of the global [B * world, H, N, D] tensors
     for t, tid in ((q, 0), (k, 1), (v, 2)):
-        ops.fill_normal_(t, args.seed, tid, 0.0, w["sigma"], index_base=rank * per)
+        ops.fill_normal_(t, args.seed, tid, 0.0, w["sigma"],
+                         index_base=rank_index_base(rank, per))
     torch.cuda.synchronize()
 
     stream = torch.cuda.current_stream()
@@ -324,10 +502,7 @@ def run_gpu_arm(args, w: dict) -> None:
     barrier()
     ops.check(stream)
     ms = start.elapsed_time(stop) / args.steps
-    t_local = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
-    ms_max = float(t_local.item())
+    ms_max = max_over_ranks(ms, world, dev)
     flops = attention_flops(w)
     value = world * flops / (ms_max * 1e-3) / 1e12
 
@@ -390,6 +565,8 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-rows", type=int, default=256,
                     help="query rows per host thread in the CPU sample")
+    ap.add_argument("--cpu-gemm-rows", type=int, default=4,
+                    help="rows of C per host thread in the CPU GEMM sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     args = ap.parse_args()
@@ -398,6 +575,8 @@ def main() -> None:
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference_arm(args, w)
+    elif w.get("kind") == "gemm":
+        run_gemm_arm(args, w)
     else:
         run_gpu_arm(args, w)
 

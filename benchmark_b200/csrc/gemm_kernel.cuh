@@ -48,6 +48,8 @@ struct Params {
   int M, N, K;
   int tiles_m, tiles_n, k_blocks;
   int b_col_major;  // 1: B is [N,K]; 0: B is [K,N]
+  int group_m;      // row blocks per raster group (pair kernel; 0: the kernel's default)
+  int b_stream;     // pair kernel: 1 = B loads hint L2 evict_first (read by one wave only)
   uint16_t* C;
 };
 
@@ -341,11 +343,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
     // ================= TMA producer (both CTAs) =================
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_last();
+      const uint64_t pol_b = p.b_stream ? l2_policy_evict_first() : pol;
+      const int group = p.group_m > 0 ? p.group_m : kGroupM;
       int it = 0, issued_last = -1;
       bool ok = true;
       for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
         int mb, nb;
-        tile_coords(p, t, kGroupM, &mb, &nb);
+        tile_coords(p, t, group, &mb, &nb);
         const int arow = mb * kBM + static_cast<int>(rank) * kHalf;
         const int brow = nb * kBN + static_cast<int>(rank) * kHalf;
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
@@ -359,11 +363,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
           const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
           tma_load_2d_pair(sa, &a_map, fb, kb * kBK, arow, pol);
           if (p.b_col_major) {
-            tma_load_2d_pair(sb, &b_map, fb, kb * kBK, brow, pol);
+            tma_load_2d_pair(sb, &b_map, fb, kb * kBK, brow, pol_b);
           } else {
 #pragma unroll
             for (int h = 0; h < kHalf / 64; ++h)
-              tma_load_2d_pair(sb + h * (kBK * 128), &b_map, fb, brow + h * 64, kb * kBK, pol);
+              tma_load_2d_pair(sb + h * (kBK * 128), &b_map, fb, brow + h * 64, kb * kBK,
+                               pol_b);
           }
           issued_last = it;
         }
@@ -381,7 +386,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // ================= MMA issuer (even CTA) =================
-    if (leader && lane == 0) {
+    // The whole warp runs the loop (operands stay warp-uniform); one elected
+    // lane issues each MMA and commit.
+    if (leader) {
       constexpr uint32_t idesc_k = idesc_bf16_f32(kBM, kBN, false, false);
       constexpr uint32_t idesc_mn = idesc_bf16_f32(kBM, kBN, false, true);
       const uint32_t idesc = p.b_col_major ? idesc_k : idesc_mn;
@@ -393,26 +400,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
       bool ok = true;
       for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++lt) {
         const int a = lt & 1;
-        ok = mbar_wait(&acc_empty[a], (static_cast<uint32_t>(lt >> 1) & 1u) ^ 1u, kSiteAccEmpty);
+        ok = __all_sync(0xffffffffu, mbar_wait(&acc_empty[a],
+                                               (static_cast<uint32_t>(lt >> 1) & 1u) ^ 1u,
+                                               kSiteAccEmpty));
         if (!ok) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(a * kBN);
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const int s = it % kStages;
-          ok = mbar_wait(&full[s], static_cast<uint32_t>(it / kStages) & 1u, kSiteFull);
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&full[s], static_cast<uint32_t>(it / kStages) & 1u, kSiteFull));
           if (!ok) break;
           tc_fence_after();
           const uint64_t da = da0 + s * (kStageBytes >> 4);
           const uint64_t db = db0 + s * (kStageBytes >> 4);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
-            mma_ss_pair(d_tmem, da + k * 2, db + k * b_step, idesc, (kb | k) > 0 ? 1u : 0u);
-          mma_commit_pair_both(&empty[s], 0x3);
+            mma_ss_pair_warp(d_tmem, da + k * 2, db + k * b_step, idesc, (kb | k) > 0 ? 1u : 0u);
+          mma_commit_pair_both_warp(&empty[s], 0x3);
         }
         if (!ok) break;
-        mma_commit_pair_both(&acc_full[a], 0x3);
+        mma_commit_pair_both_warp(&acc_full[a], 0x3);
       }
-      mma_commit_pair_local(drain);
+      if (lane == 0) mma_commit_pair_local(drain);
+      __syncwarp();
       drain_wait(drain, 0);
     }
     __syncwarp();
@@ -425,7 +436,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
     for (int t = cluster_id; t < num_tiles; t += num_clusters, ++lt) {
       const int a = lt & 1;
       int mb, nb;
-      tile_coords(p, t, kGroupM, &mb, &nb);
+      tile_coords(p, t, p.group_m > 0 ? p.group_m : kGroupM, &mb, &nb);
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[a],
                                                         static_cast<uint32_t>(lt >> 1) & 1u,
                                                         kSiteAccFull));

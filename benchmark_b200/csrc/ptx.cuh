@@ -428,6 +428,27 @@ __device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar, uint16_t cta
       : "memory");
 }
 
+// Warp-converged forms: the whole warp executes them with the same operands
+// and one elected lane issues.
+__device__ __forceinline__ void mma_ss_pair_warp(uint32_t d_tmem, uint64_t a_desc,
+                                                 uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_pair_both_warp(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;\n}\n" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
 // Same, for an mbarrier of the issuing CTA only.
 __device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
   asm volatile(
