@@ -90,7 +90,7 @@ struct Params {
 enum : uint32_t {
   kEvTmaK = 1, kEvTmaV, kEvMmaS, kEvMmaPvLo, kEvMmaPvHi, kEvSmWait, kEvSmReady, kEvSmLdDone,
   kEvSmMaxDone, kEvSmPLo, kEvSmPHi, kEvEpiBegin, kEvEpiEnd, kEvMmaWait, kEvMmaEnd, kEvMmaGo,
-  kEvTmaQ
+  kEvTmaQ, kEvSmPComputed, kEvSmStored
 };
 
 template <bool kTrace>
@@ -671,6 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             p_rows<kEmu, false>(s + 32 * half, sc, nm_a, nm_b, rs_a, rs_b, pk);
           tmem_st_16x128b_x8(tS + 32 * half, pk);
         }
+        tr(kEvSmPComputed, warp >> 2, tt);
         // S(tt+1), if it is this item's and already computed: start its load.
         if (j + 1 < it.n) {
           const int nb = (tt + 1) % kSBufs;
@@ -706,6 +707,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         tmem_wait_st();
+        tr(kEvSmStored, warp >> 2, tt);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {

@@ -451,12 +451,15 @@ b200_status launch_gemm_single(const void* A, const void* Bm, void* C, int M, in
   return B200_OK;
 }
 
-// Raster group (256-row blocks per group) and B's L2 hint for the pair
-// kernel; B200_GEMM_GROUP_M / B200_GEMM_B_STREAM override them for sweeps.
-// Measured on B200 (B [K,N]): groups of 8 are best at 8192^3 (16 costs 0.4 %),
-// groups of 16 at 16384^3 (+2 % over 8); an evict-first hint on B loses 1-8 %.
+// Raster group (256-row blocks per group) and the L2 hints of the pair
+// kernel's A and B loads (0 evict_last, 1 evict_first, 2 evict_normal);
+// B200_GEMM_GROUP_M / B200_GEMM_A_POLICY / B200_GEMM_B_POLICY override them
+// for sweeps.  Measured on B200 (B [K,N]): groups of 8 are best at 8192^3
+// (16 costs 0.4 %), groups of 16 at 16384^3 (+2 % over 8); an evict-first
+// hint on B loses 1-8 %.
 int gemm_default_group(int K) { return K >= 12288 ? 16 : 8; }
-constexpr int kGemmBStream = 0;
+constexpr int kGemmAPolicy = 0;
+constexpr int kGemmBPolicy = 0;
 
 int gemm_env_int(const char* name, int fallback) {
   const char* e = std::getenv(name);
@@ -503,7 +506,8 @@ b200_status launch_gemm_pair(const void* A, const void* Bm, void* C, int M, int 
   if (st != B200_OK) return st;
   g::Params p = gemm_params(M, N, K, b_col_major, C, g::pair::kBM, g::pair::kBN, g::pair::kBK);
   p.group_m = gemm_env_int("B200_GEMM_GROUP_M", gemm_default_group(K));
-  p.b_stream = gemm_env_int("B200_GEMM_B_STREAM", kGemmBStream);
+  p.a_policy = gemm_env_int("B200_GEMM_A_POLICY", kGemmAPolicy);
+  p.b_policy = gemm_env_int("B200_GEMM_B_POLICY", kGemmBPolicy);
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
   if (tiles > 0x3fffffffll) return fail(B200_EUNSUPPORTED, "gemm_bf16: too many tiles");
   const long long clusters = std::min<long long>(tiles, pair_clusters_resident());

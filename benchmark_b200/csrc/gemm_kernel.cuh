@@ -49,7 +49,8 @@ struct Params {
   int tiles_m, tiles_n, k_blocks;
   int b_col_major;  // 1: B is [N,K]; 0: B is [K,N]
   int group_m;      // row blocks per raster group (pair kernel; 0: the kernel's default)
-  int b_stream;     // pair kernel: 1 = B loads hint L2 evict_first (read by one wave only)
+  int a_policy;     // pair kernel L2 hints for A and B loads:
+  int b_policy;     //   0 evict_last, 1 evict_first, 2 evict_normal
   uint16_t* C;
 };
 
@@ -342,8 +343,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
   if (warp == kTmaWarp) {
     // ================= TMA producer (both CTAs) =================
     if (lane == 0) {
-      const uint64_t pol = l2_policy_evict_last();
-      const uint64_t pol_b = p.b_stream ? l2_policy_evict_first() : pol;
+      auto policy = [](int k) {
+        return k == 1 ? l2_policy_evict_first()
+                      : (k == 2 ? l2_policy_evict_normal() : l2_policy_evict_last());
+      };
+      const uint64_t pol = policy(p.a_policy);
+      const uint64_t pol_b = policy(p.b_policy);
       const int group = p.group_m > 0 ? p.group_m : kGroupM;
       int it = 0, issued_last = -1;
       bool ok = true;

@@ -25,7 +25,7 @@ from . import _lib, ops
 EVENTS = {1: "tma_k", 2: "tma_v", 3: "mma_s", 4: "mma_pv_lo", 5: "mma_pv_hi", 6: "sm_wait",
           7: "sm_ready", 8: "sm_ld_done", 9: "sm_max_done", 10: "sm_p_lo", 11: "sm_p_hi",
           12: "epi_begin", 13: "epi_end", 14: "mma_wait", 15: "mma_end", 16: "mma_go",
-          17: "tma_q"}
+          17: "tma_q", 18: "sm_p_computed", 19: "sm_p_stored"}
 ROLES = {0: "tma", 1: "mma", 2: "softmax0", 3: "softmax1", 4: "epilogue"}
 
 
@@ -72,13 +72,16 @@ def summarize(recs):
         iters = sorted({r["iter"] for r in recs if r["role"] == role})
         for j in iters:
             g = {e: at.get((role, e, h, j)) for e in
-                 ("sm_wait", "sm_ld_done", "sm_max_done", "sm_p_lo")}
+                 ("sm_wait", "sm_ld_done", "sm_max_done", "sm_p_lo", "sm_p_computed",
+                  "sm_p_stored")}
             if None in g.values():
                 continue
             p_done = g["sm_p_lo"]
             stages[f"{role}.wait_s+ld"].append(g["sm_ld_done"] - g["sm_wait"])
             stages[f"{role}.max"].append(g["sm_max_done"] - g["sm_ld_done"])
-            stages[f"{role}.p"].append(p_done - g["sm_max_done"])
+            stages[f"{role}.p_compute"].append(g["sm_p_computed"] - g["sm_max_done"])
+            stages[f"{role}.prefetch+rescale"].append(g["sm_p_stored"] - g["sm_p_computed"])
+            stages[f"{role}.arrive"].append(p_done - g["sm_p_stored"])
             nxt = at.get((role, "sm_wait", h, j + 1))
             if nxt is not None:
                 stages[f"{role}.period"].append(nxt - g["sm_wait"])
