@@ -433,6 +433,7 @@ def run_gemm_arm(args, w: dict) -> None:
                    "parallelism": f"dp{world} (independent GEMM per rank)",
                    "l2": "inputs larger than L2 (256 MiB of A and B per step)"},
         "cublas_tflops": world * flops / (ms_cublas * 1e-3) / 1e12,
+        "hbm_gbs_algorithmic": world * 2 * (M * K + K * N + M * N) / (ms_max * 1e-3) / 1e9,
         "vs_cublas": ms_cublas / ms_max,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES.get(args.workload),
@@ -540,6 +541,11 @@ def run_gpu_arm(args, w: dict) -> None:
                    "l2": (f"inputs larger than L2 ({3 * q.numel() * 2 / 2**20:.0f} MiB of "
                           "Q/K/V read per step)")},
         "per_gpu_tflops": value / world,
+        # algorithmic HBM rate (Q+K+V read, O written once) and exp2 rate,
+        # whole box: the config-4 view of the same run
+        "hbm_gbs_algorithmic": world * algo_bytes / (ms_max * 1e-3) / 1e9,
+        "exp_per_s": world * (w["b"] * w["h"] * w["n"] * w["n"] / (2 if w["causal"] else 1))
+        / (ms_max * 1e-3),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "algorithmic_bytes": algo_bytes,

@@ -33,10 +33,10 @@
 // every scheduler without any cross-warp barrier.
 //
 // MMA issue order over the global tile stream t (crossing item boundaries):
-//   S(0), S(1), then for every t: S(t+2), PV(t)   (PV(t) in two 64-key
-//   halves, each issued when all eight softmax warps have stored that half
-//   of P(t)).  S(t+3) overwrites P(t) after PV(t) in issue order; the tensor
-//   pipe executes one thread's MMAs in issue order.
+//   S(0), S(1), then for every t: S(t+2), PV(t)   (PV(t) issued once all
+//   eight softmax warps have stored P(t)).  S(t+3) overwrites P(t) after
+//   PV(t) in issue order; the tensor pipe executes one thread's MMAs in
+//   issue order.
 //
 // Softmax per tile: a thread reads 32 scores of each of its two rows
 // (16x256b TMEM loads), the row max is completed by two shuffles, and the
@@ -77,6 +77,7 @@ struct Params {
   int causal;      // bottom-right aligned
   int causal_off;  // Skv - Sq
   float scale_log2;  // softmax_scale * log2(e)
+  int stagger_cycles;  // start delay of softmax warps 4-7 (bounded, clock64 cycles)
   // Clock trace (kTrace instantiations only): per-role record regions of
   // trace_cap records (2 x u64: (event << 32 | tile << 24 | iter), clock64)
   // for CTA trace_cta.  Role r (0 TMA, 1 MMA, 2/3 softmax keys 0-63/64-127,
@@ -131,8 +132,8 @@ struct Cfg {
   static constexpr int kFlagOff = kLOff + 2 * 128 * 4;        // abort flag (epilogue)
   static constexpr int kBarOff = kFlagOff + 16;
   // q_full[2] q_empty[2] k_full[K] k_empty[K] v_full[V] v_empty[V]
-  // s_ready[3] p_lo[3] p_hi[3] pv_done o_full o_empty l_ready[2] drain done
-  static constexpr int kNumBars = 4 + 2 * kKStages + 2 * kVStages + 3 * kSBufs + 1 + 4 + 2;
+  // s_ready[3] p_ready[3] pv_done o_full o_empty l_ready[2] drain done
+  static constexpr int kNumBars = 4 + 2 * kKStages + 2 * kVStages + 2 * kSBufs + 1 + 4 + 2;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kTmemSlotOff + 16 + 1024;  // + 1 KiB alignment slack
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB of shared memory a CTA may use");
@@ -277,9 +278,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_full = k_empty + C::kKStages;
   uint64_t* v_empty = v_full + C::kVStages;
   uint64_t* s_ready = v_empty + C::kVStages;
-  uint64_t* p_lo = s_ready + kSBufs;
-  uint64_t* p_hi = p_lo + kSBufs;
-  uint64_t* pv_done = p_hi + kSBufs;
+  uint64_t* p_ready = s_ready + kSBufs;
+  uint64_t* pv_done = p_ready + kSBufs;
   uint64_t* o_full = pv_done + 1;
   uint64_t* o_empty = o_full + 1;
   uint64_t* l_ready = o_empty + 1;
@@ -300,8 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < kSBufs; ++i) {
       mbar_init(&s_ready[i], 1);
-      mbar_init(&p_lo[i], 8);
-      mbar_init(&p_hi[i], 8);
+      mbar_init(&p_ready[i], 8);
     }
     mbar_init(o_full, 1);
     mbar_init(o_empty, 128);
@@ -525,12 +524,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = wait3(bar(o_empty), oe_par, dn_a, dn_p, dn_a, dn_p, kSiteOEmpty);
             if (!ok) break;
           }
-          ok = wait3(bar(&v_full[tt % C::kVStages]), vpar(tt), bar(&p_lo[tt % kSBufs]), tpar,
+          // One grouped wait per PV: polls cost a few hundred cycles each,
+          // and S(t+2), issued just before, keeps the tensor pipe busy
+          // meanwhile.
+          ok = wait3(bar(&v_full[tt % C::kVStages]), vpar(tt), bar(&p_ready[tt % kSBufs]), tpar,
                      dn_a, dn_p, kSitePReady);
           if (!ok) break;
           issue_pv_half(tt, j == 0, 0);
-          ok = wait3(bar(&p_hi[tt % kSBufs]), tpar, dn_a, dn_p, dn_a, dn_p, kSitePReady);
-          if (!ok) break;
           issue_pv_half(tt, j == 0, 1);
           mma_commit_warp(&v_empty[tt % C::kVStages]);
           mma_commit_warp(pv_done);
@@ -562,6 +562,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     Tracer<kTrace> tr(p, 2 + static_cast<int>(warp >> 2), trace_cta && quad == 0 && lane == 0);
     int t = 0, li = 0;
     bool ok = true;
+    // Warps w and w+4 share a scheduler and would otherwise run their exp2
+    // phases in lockstep; starting the second one a part-tile later lets one
+    // warp's exp2 overlap the other's loads, max and bookkeeping.
+    if ((warp >> 2) != 0 && p.stagger_cycles > 0) {
+      const long long t_start = clock64();
+      while (clock64() - t_start < p.stagger_cycles) {
+      }
+    }
 #pragma unroll 1
     for (int r = 0; r < rounds && ok; ++r) {
       const int k = item_index(p, r);
@@ -638,6 +646,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
         mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
         tr(kEvSmMaxDone, warp >> 2, tt);
+        if (j > 0) {
+          // P(tt-1)'s stores (and any O rescale) landed while this tile's
+          // scores were loaded and reduced: publish them now.
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_ready[(tt - 1) % kSBufs]);
+          tr(kEvSmPLo, warp >> 2, tt - 1);
+        }
 
         // Running-max update with lazy rescaling (per row; the four threads
         // of a row hold the same values, so they decide alike).
@@ -706,21 +723,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        tmem_wait_st();
         tr(kEvSmStored, warp >> 2, tt);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&p_lo[sb]);
-          mbar_arrive(&p_hi[sb]);
-        }
-        tr(kEvSmPLo, warp >> 2, tt);
         float r0, r1;
         f2_unpack(rs_a, r0, r1);
         l_a = l_a * f_a + (r0 + r1);
         f2_unpack(rs_b, r0, r1);
         l_b = l_b * f_b + (r0 + r1);
         if (!ok) break;
+      }
+      if (ok && it.n > 0) {
+        // The item's last P.
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_ready[(t + it.n - 1) % kSBufs]);
+        tr(kEvSmPLo, warp >> 2, t + it.n - 1);
       }
       if (have_s) {
         // Abandoned prefetch (only after an abort): let the load land.
