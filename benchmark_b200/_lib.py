@@ -44,6 +44,8 @@ _PROTOTYPES = {
     "gemm_bf16": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "gemm_bf16_cublas": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "gemm_f32_reference": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
+    "gemm_cublas_mode": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
+    "b200_fill_cublas_pattern": [_vp, _u64, _i, _f, _vp],
 }
 
 

@@ -18,6 +18,8 @@
 #include "gemm_kernel.cuh"
 
 #include <cublas_v2.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <map>
 
 namespace {
@@ -556,6 +558,65 @@ extern "C" b200_status gemm_bf16_cublas(const void* A, const void* Bm, void* C, 
       h, b_col_major ? CUBLAS_OP_T : CUBLAS_OP_N, CUBLAS_OP_N, N, M, K, &alpha, Bm, CUDA_R_16BF,
       b_col_major ? K : N, A, CUDA_R_16BF, K, &beta, C, CUDA_R_16BF, N, CUBLAS_COMPUTE_32F,
       CUBLAS_GEMM_DEFAULT);
+  if (r != CUBLAS_STATUS_SUCCESS) return fail(B200_ECUDA, "cublasGemmEx failed (%d)", (int)r);
+  return B200_OK;
+}
+
+namespace {
+__global__ void fill_cublas_pattern_kernel(void* dst, uint64_t n, int mode, float scale) {
+  const uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+  if (i >= n) return;
+  const float v = (static_cast<float>(i % 251) - 125.0f) * scale;
+  if (mode == B200_CUBLAS_FP16)
+    static_cast<__half*>(dst)[i] = __float2half_rn(v);
+  else if (mode == B200_CUBLAS_BF16)
+    static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(v);
+  else
+    static_cast<float*>(dst)[i] = v;
+}
+}  // namespace
+
+extern "C" b200_status b200_fill_cublas_pattern(void* dst, uint64_t n, int mode, float scale,
+                                                b200_stream_t stream) {
+  if (mode < B200_CUBLAS_FP16 || mode > B200_CUBLAS_FP32)
+    return fail(B200_EINVAL, "b200_fill_cublas_pattern: unknown mode %d", mode);
+  if (n == 0) return B200_OK;
+  if (!dst) return fail(B200_EINVAL, "b200_fill_cublas_pattern: null pointer");
+  const uint64_t blocks = (n + 255) / 256;
+  if (blocks > 0x7fffffffull) return fail(B200_EUNSUPPORTED, "b200_fill_cublas_pattern: too big");
+  fill_cublas_pattern_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                               reinterpret_cast<cudaStream_t>(stream)>>>(dst, n, mode, scale);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "b200_fill_cublas_pattern launch");
+  return B200_OK;
+}
+
+extern "C" b200_status gemm_cublas_mode(const void* A, const void* Bm, void* C, int M, int N,
+                                        int K, int mode, b200_stream_t stream) {
+  if (!A || !Bm || !C) return fail(B200_EINVAL, "gemm_cublas_mode: null matrix pointer");
+  if (M < 1 || N < 1 || K < 1) return fail(B200_EINVAL, "gemm_cublas_mode: invalid shape");
+  cudaDataType_t type;
+  cublasComputeType_t compute;
+  cublasGemmAlgo_t algo = CUBLAS_GEMM_DEFAULT_TENSOR_OP;
+  switch (mode) {
+    case B200_CUBLAS_FP16: type = CUDA_R_16F; compute = CUBLAS_COMPUTE_32F; break;
+    case B200_CUBLAS_BF16: type = CUDA_R_16BF; compute = CUBLAS_COMPUTE_32F; break;
+    case B200_CUBLAS_TF32: type = CUDA_R_32F; compute = CUBLAS_COMPUTE_32F_FAST_TF32; break;
+    case B200_CUBLAS_FP32:
+      type = CUDA_R_32F;
+      compute = CUBLAS_COMPUTE_32F_PEDANTIC;
+      algo = CUBLAS_GEMM_DEFAULT;
+      break;
+    default: return fail(B200_EINVAL, "gemm_cublas_mode: unknown mode %d", mode);
+  }
+  b200_status st = B200_OK;
+  cublasHandle_t h = cublas_handle(&st);
+  if (!h) return st;
+  if (cublasSetStream(h, reinterpret_cast<cudaStream_t>(stream)) != CUBLAS_STATUS_SUCCESS)
+    return fail(B200_ECUDA, "cublasSetStream failed");
+  const float alpha = 1.0f, beta = 0.0f;
+  const cublasStatus_t r = cublasGemmEx(h, CUBLAS_OP_N, CUBLAS_OP_N, M, N, K, &alpha, A, type, M,
+                                        Bm, type, K, &beta, C, type, M, compute, algo);
   if (r != CUBLAS_STATUS_SUCCESS) return fail(B200_ECUDA, "cublasGemmEx failed (%d)", (int)r);
   return B200_OK;
 }

@@ -102,6 +102,31 @@ b200_status gemm_bf16_cublas(const void* A, const void* B, void* C, int M, int N
                              int b_col_major, b200_stream_t stream);
 
 /*
+ * The reference's cuBLAS benchmark in each of its modes
+ * (6.cuBLAS/cublas_gemm_bench.cu:145-166, call :226-231): column-major
+ * C[M,N] = A[M,K] B[K,N] with lda = M, ldb = K, ldc = M, no transposes.
+ * Element type of A, B and C by mode: fp16 / bf16 (2 bytes, fp32
+ * accumulate), tf32 (fp32 storage, TF32 tensor cores), fp32 (CUDA cores,
+ * pedantic).  Comparator only: timed, never used on the product path.
+ */
+typedef enum {
+  B200_CUBLAS_FP16 = 0,
+  B200_CUBLAS_BF16 = 1,
+  B200_CUBLAS_TF32 = 2,
+  B200_CUBLAS_FP32 = 3
+} b200_cublas_mode;
+
+b200_status gemm_cublas_mode(const void* A, const void* B, void* C, int M, int N, int K,
+                             int mode, b200_stream_t stream);
+
+/*
+ * The cuBLAS benchmark's input pattern, value i = ((i % 251) - 125) * scale
+ * in the mode's element type (6.cuBLAS/cublas_gemm_bench.cu:28-58).
+ */
+b200_status b200_fill_cublas_pattern(void* dst, uint64_t n, int mode, float scale,
+                                     b200_stream_t stream);
+
+/*
  * Validation-only fp32 CUDA-core GEMM: C[M,N] fp32 row-major.  GPU analogue
  * of the reference's double-precision CPU loop
  * (5.GEMM/gemm256_tma_tcgen05_bench.cu:1115-1137) for full-size checks.

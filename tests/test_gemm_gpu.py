@@ -114,3 +114,36 @@ def test_cublas_comparator_matches_oracle():
     ops.check()
     ref = oracle.gemm(bits(a), bits(b), True)
     assert rel_frob(c.float().cpu().numpy(), ref) <= FROB
+
+
+@pytest.mark.parametrize("mode,dtype,tol", [(0, torch.float16, 2e-3), (1, torch.bfloat16, 1e-2),
+                                            (2, torch.float32, 2e-3), (3, torch.float32, 1e-6)])
+def test_cublas_modes_match_oracle(mode, dtype, tol):
+    """gemm_cublas_mode: column-major C = A B in 6.cuBLAS's four modes, against
+    the oracle's double-precision loop on the same (rounded) inputs."""
+    from benchmark_b200 import _lib
+    M, N, K = 192, 160, 256
+    g = torch.Generator().manual_seed(5 + mode)
+    a_rm = (torch.rand(M, K, generator=g) * 2 - 1).to(dtype)  # row-major [M,K]
+    b_rm = (torch.rand(K, N, generator=g) * 2 - 1).to(dtype)  # row-major [K,N]
+    # column-major storage = transposed row-major buffers
+    a_cm = a_rm.t().contiguous().cuda()
+    b_cm = b_rm.t().contiguous().cuda()
+    c_cm = torch.empty((N, M), dtype=dtype, device="cuda")
+    _lib.call("gemm_cublas_mode", a_cm.data_ptr(), b_cm.data_ptr(), c_cm.data_ptr(), M, N, K,
+              mode, torch.cuda.current_stream().cuda_stream)
+    ops.check()
+    got = c_cm.t().float().cpu().numpy()
+    ref = a_rm.double().numpy() @ b_rm.double().numpy()
+    assert rel_frob(got, ref) <= tol, rel_frob(got, ref)
+
+
+def test_cublas_pattern_fill():
+    from benchmark_b200 import _lib
+    t = torch.empty(1000, dtype=torch.float32, device="cuda")
+    _lib.call("b200_fill_cublas_pattern", t.data_ptr(), t.numel(), 3, 1e-3,
+              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    i = np.arange(1000)
+    want = ((i % 251) - 125).astype(np.float32) * np.float32(1e-3)
+    assert np.array_equal(t.cpu().numpy(), want)

@@ -11,6 +11,7 @@ import pytest
 BIN = Path(__file__).resolve().parents[1] / "benchmark_b200" / "bin"
 ATTN = BIN / "attention_bench"
 GEMM = BIN / "gemm_bench"
+CUBLAS = BIN / "cublas_bench"
 
 
 def _run(exe, *args, timeout=600):
@@ -19,7 +20,7 @@ def _run(exe, *args, timeout=600):
     return subprocess.run([str(exe), *args], capture_output=True, text=True, timeout=timeout)
 
 
-@pytest.mark.parametrize("exe", [ATTN, GEMM])
+@pytest.mark.parametrize("exe", [ATTN, GEMM, CUBLAS])
 def test_help_exits_zero(exe):
     r = _run(exe, "--help")
     assert r.returncode == 0 and "--" in r.stdout
@@ -75,3 +76,20 @@ def test_gemm_benchmark_csv(tmp_path):
     rows = list(csv.DictReader(out.open()))
     assert [int(x["size"]) for x in rows] == [1024, 2048]
     assert all(x["status"] == "ok" and float(x["event_TFLOPS"]) > 0 for x in rows)
+
+
+@pytest.mark.parametrize("args", [["--mode", "int8"], ["--m", "0"], ["--repeat", "0"],
+                                  ["--bogus"]])
+def test_cublas_bad_arguments_exit_two(args):
+    assert _run(CUBLAS, *args).returncode == 2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["fp16", "bf16", "tf32", "fp32"])
+def test_cublas_bench_modes_run(mode):
+    r = _run(CUBLAS, "--m", "1024", "--n", "512", "--k", "768", "--repeat", "3", "--warmup", "1",
+             "--mode", mode)
+    assert r.returncode == 0, r.stdout + r.stderr
+    csv_line = [ln for ln in r.stdout.splitlines() if ln.startswith("csv,")]
+    assert len(csv_line) == 1 and csv_line[0].split(",")[1] == mode
+    assert float(csv_line[0].split(",")[8]) > 0
