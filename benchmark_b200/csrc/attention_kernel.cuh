@@ -255,6 +255,43 @@ __device__ __forceinline__ void p_rows(const float* s, float sc, float nm_a, flo
   }
 }
 
+// p_rows for an unmasked block against a running max that may be stale:
+// also reduces the max of x over the block per row (mx_a, mx_b), on the ALU
+// pipe while the exponentials occupy MUFU.
+template <int kEmu>
+__device__ __forceinline__ void p_rows_max(const float* s, float sc, float nm_a, float nm_b,
+                                           uint64_t& rs_a, uint64_t& rs_b, uint32_t (&pk)[16],
+                                           float& mx_a, float& mx_b) {
+  const uint64_t sc2 = f2_pack(sc, sc);
+  const uint64_t na2 = f2_pack(nm_a, nm_a);
+  const uint64_t nb2 = f2_pack(nm_b, nm_b);
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint64_t x2 = f2_fma(f2_pack(s[4 * g + 2 * rr], s[4 * g + 2 * rr + 1]), sc2,
+                                 rr ? nb2 : na2);
+      float x0, x1, p0, p1;
+      f2_unpack(x2, x0, x1);
+      if (rr)
+        mx_b = fmax3(mx_b, x0, x1);
+      else
+        mx_a = fmax3(mx_a, x0, x1);
+      if (((2 * g + rr) & 7) < kEmu) {
+        exp2_fma_x2(x0, x1, p0, p1);
+      } else {
+        p0 = ex2_approx(x0);
+        p1 = ex2_approx(x1);
+      }
+      if (rr)
+        rs_b = f2_add(rs_b, f2_pack(p0, p1));
+      else
+        rs_a = f2_add(rs_a, f2_pack(p0, p1));
+      pk[2 * g + rr] = pack_bf16x2(p0, p1);
+    }
+  }
+}
+
 template <int D, int kEmu, bool kTrace = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_fwd_kernel(const __grid_constant__ CUtensorMap q_map,
@@ -607,86 +644,137 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* s = reinterpret_cast<float*>(sr);
         const int kbase = j * kBN;
         const bool masked = kbase + kBN > it.min_lim;  // uniform across the tile
-        float mx_a, mx_b;
-        if (masked) {
-          // Scale first, then mask, so masked keys are exactly -inf for any scale.
-          const int va = lim_a - kbase - 2 * t0, vb = lim_b - kbase - 2 * t0;
-          mx_a = -INFINITY;
-          mx_b = -INFINITY;
-#pragma unroll
-          for (int g = 0; g < 16; ++g) {
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const float xa = 8 * g + e < va ? s[4 * g + e] * c : -INFINITY;
-              const float xb = 8 * g + e < vb ? s[4 * g + 2 + e] * c : -INFINITY;
-              s[4 * g + e] = xa;
-              s[4 * g + 2 + e] = xb;
-              mx_a = fmaxf(mx_a, xa);
-              mx_b = fmaxf(mx_b, xb);
-            }
-          }
-        } else {
-          // Four independent chains per row over the 16 repeats.
-          float a[4], b[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            a[u] = fmaxf(s[4 * u], s[4 * u + 1]);
-            b[u] = fmaxf(s[4 * u + 2], s[4 * u + 3]);
-          }
-#pragma unroll
-          for (int g = 4; g < 16; ++g) {
-            a[g & 3] = fmax3(a[g & 3], s[4 * g], s[4 * g + 1]);
-            b[g & 3] = fmax3(b[g & 3], s[4 * g + 2], s[4 * g + 3]);
-          }
-          mx_a = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])) * c;
-          mx_b = fmaxf(fmaxf(b[0], b[1]), fmaxf(b[2], b[3])) * c;
-        }
-        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
-        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
-        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
-        tr(kEvSmMaxDone, warp >> 2, tt);
-        if (j > 0) {
+        float f_a = 1.0f, f_b = 1.0f;
+        bool rescale = false;
+        uint64_t rs_a = 0ull, rs_b = 0ull;
+        // A later unmasked tile of rows that already have a finite running max
+        // computes P against that max at once and reduces max(x) in the same
+        // loop; only when some row's max rose by more than 2^kRescaleLog2
+        // (rare) is P recomputed against the new max.  Same results as taking
+        // the max first: m only moves when the block raises it past the
+        // threshold, and then to the block max.
+        const bool spec =
+            !masked && j > 0 && __all_sync(0xffffffffu, m_a != -INFINITY && m_b != -INFINITY);
+        if (spec) {
           // P(tt-1)'s stores (and any O rescale) landed while this tile's
-          // scores were loaded and reduced: publish them now.
+          // scores were loaded: publish them now.
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&p_ready[(tt - 1) % kSBufs]);
           tr(kEvSmPLo, warp >> 2, tt - 1);
-        }
-
-        // Running-max update with lazy rescaling (per row; the four threads
-        // of a row hold the same values, so they decide alike).
-        float f_a = 1.0f, f_b = 1.0f;
-        bool rescale = false;
-        if (m_a == -INFINITY) {
-          m_a = mx_a;  // no probability mass accumulated yet for this row
-        } else if (mx_a > m_a + kRescaleLog2) {
-          f_a = ex2_approx(m_a - mx_a);
-          m_a = mx_a;
-          rescale = true;
-        }
-        if (m_b == -INFINITY) {
-          m_b = mx_b;
-        } else if (mx_b > m_b + kRescaleLog2) {
-          f_b = ex2_approx(m_b - mx_b);
-          m_b = mx_b;
-          rescale = true;
-        }
-        const float nm_a = (m_a == -INFINITY) ? 0.0f : -m_a;
-        const float nm_b = (m_b == -INFINITY) ? 0.0f : -m_b;
-        const float sc = masked ? 1.0f : c;  // masked scores are pre-scaled
-        uint64_t rs_a = 0ull, rs_b = 0ull;
-        // P for keys 0-63 (repeats g = 0..7), then 64-127 (g = 8..15).
+          float xa = -INFINITY, xb = -INFINITY;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[16];
-          if (masked)
-            p_rows<kEmu, true>(s + 32 * half, sc, nm_a, nm_b, rs_a, rs_b, pk);
-          else
-            p_rows<kEmu, false>(s + 32 * half, sc, nm_a, nm_b, rs_a, rs_b, pk);
-          tmem_st_16x128b_x8(tS + 32 * half, pk);
+          for (int half = 0; half < 2; ++half) {
+            uint32_t pk[16];
+            p_rows_max<kEmu>(s + 32 * half, c, -m_a, -m_b, rs_a, rs_b, pk, xa, xb);
+            tmem_st_16x128b_x8(tS + 32 * half, pk);
+          }
+          xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 1));
+          xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 1));
+          xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 2));
+          xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 2));
+          tr(kEvSmMaxDone, warp >> 2, tt);
+          if (xa > kRescaleLog2) {
+            f_a = ex2_approx(-xa);
+            m_a += xa;
+            rescale = true;
+          }
+          if (xb > kRescaleLog2) {
+            f_b = ex2_approx(-xb);
+            m_b += xb;
+            rescale = true;
+          }
+          if (__any_sync(0xffffffffu, rescale)) {
+            // Rare: redo P against the raised maxima.
+            tmem_wait_st();
+            rs_a = 0ull;
+            rs_b = 0ull;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              uint32_t pk[16];
+              p_rows<kEmu, false>(s + 32 * half, c, -m_a, -m_b, rs_a, rs_b, pk);
+              tmem_st_16x128b_x8(tS + 32 * half, pk);
+            }
+          }
+        } else {
+          float mx_a, mx_b;
+          if (masked) {
+            // Scale first, then mask, so masked keys are exactly -inf for any scale.
+            const int va = lim_a - kbase - 2 * t0, vb = lim_b - kbase - 2 * t0;
+            mx_a = -INFINITY;
+            mx_b = -INFINITY;
+#pragma unroll
+            for (int g = 0; g < 16; ++g) {
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const float xa = 8 * g + e < va ? s[4 * g + e] * c : -INFINITY;
+                const float xb = 8 * g + e < vb ? s[4 * g + 2 + e] * c : -INFINITY;
+                s[4 * g + e] = xa;
+                s[4 * g + 2 + e] = xb;
+                mx_a = fmaxf(mx_a, xa);
+                mx_b = fmaxf(mx_b, xb);
+              }
+            }
+          } else {
+            // Four independent chains per row over the 16 repeats.
+            float a[4], b[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              a[u] = fmaxf(s[4 * u], s[4 * u + 1]);
+              b[u] = fmaxf(s[4 * u + 2], s[4 * u + 3]);
+            }
+#pragma unroll
+            for (int g = 4; g < 16; ++g) {
+              a[g & 3] = fmax3(a[g & 3], s[4 * g], s[4 * g + 1]);
+              b[g & 3] = fmax3(b[g & 3], s[4 * g + 2], s[4 * g + 3]);
+            }
+            mx_a = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])) * c;
+            mx_b = fmaxf(fmaxf(b[0], b[1]), fmaxf(b[2], b[3])) * c;
+          }
+          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+          tr(kEvSmMaxDone, warp >> 2, tt);
+          if (j > 0) {
+            // P(tt-1)'s stores (and any O rescale) landed while this tile's
+            // scores were loaded and reduced: publish them now.
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_ready[(tt - 1) % kSBufs]);
+            tr(kEvSmPLo, warp >> 2, tt - 1);
+          }
+          // Running-max update with lazy rescaling (per row; the four
+          // threads of a row hold the same values, so they decide alike).
+          if (m_a == -INFINITY) {
+            m_a = mx_a;  // no probability mass accumulated yet for this row
+          } else if (mx_a > m_a + kRescaleLog2) {
+            f_a = ex2_approx(m_a - mx_a);
+            m_a = mx_a;
+            rescale = true;
+          }
+          if (m_b == -INFINITY) {
+            m_b = mx_b;
+          } else if (mx_b > m_b + kRescaleLog2) {
+            f_b = ex2_approx(m_b - mx_b);
+            m_b = mx_b;
+            rescale = true;
+          }
+          const float nm_a = (m_a == -INFINITY) ? 0.0f : -m_a;
+          const float nm_b = (m_b == -INFINITY) ? 0.0f : -m_b;
+          const float sc = masked ? 1.0f : c;  // masked scores are pre-scaled
+          // P for keys 0-63 (repeats g = 0..7), then 64-127 (g = 8..15).
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t pk[16];
+            if (masked)
+              p_rows<kEmu, true>(s + 32 * half, sc, nm_a, nm_b, rs_a, rs_b, pk);
+            else
+              p_rows<kEmu, false>(s + 32 * half, sc, nm_a, nm_b, rs_a, rs_b, pk);
+            tmem_st_16x128b_x8(tS + 32 * half, pk);
+          }
         }
         tr(kEvSmPComputed, warp >> 2, tt);
         // S(tt+1), if it is this item's and already computed: start its load.
