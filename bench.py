@@ -58,7 +58,7 @@ WORKLOADS = {
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel,
 # from the ncu capture in profiles/attention_fwd_d128_c2_b4h32n4096.md (None: not captured).
-NCU_TRAFFIC_BYTES = {"c2": 517.65e6}
+NCU_TRAFFIC_BYTES = {"c2": 515.65e6, "gemm": 1152.5e6}
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -519,10 +519,11 @@ def run_gpu_arm(args, w: dict) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = host_threads()
-        r = cpu_reference_sample(w, args.cpu_rows, threads)
+        rows = args.cpu_baseline_rows
+        r = cpu_reference_sample(w, rows, threads)
         cpu = {"value": r["flops"] / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": threads,
                "kind": r["kind"],
-               "sample": (f"{threads} threads x {args.cpu_rows} query rows x {N} keys x d{D} "
+               "sample": (f"{threads} threads x {rows} query rows x {N} keys x d{D} "
                           f"({r['seconds']:.1f} s wall)")}
 
     if world > 1:
@@ -570,7 +571,10 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-rows", type=int, default=256,
-                    help="query rows per host thread in the CPU sample")
+                    help="query rows per host thread in each --impl reference step")
+    ap.add_argument("--cpu-baseline-rows", type=int, default=4096,
+                    help="query rows per host thread in the GPU line's cpu_baseline "
+                         "(about 10 s of host work at config 2)")
     ap.add_argument("--cpu-gemm-rows", type=int, default=4,
                     help="rows of C per host thread in the CPU GEMM sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
