@@ -84,6 +84,18 @@ def build_harness(verbose: bool = False, force: bool = False) -> list[Path]:
                f"-L{PKG}", "-lb200attn", f"-Xlinker=-rpath,$ORIGIN/..", "-lcudart", "-lpthread"]
         _run(cmd, verbose)
         built.append(exe)
+    # Device-code tools (the peak probes): sm_100a, self-contained.
+    csrc_h = sorted(CSRC.glob("*.cuh"))
+    for src in sorted(HARNESS_SRC.glob("*.cu")):
+        exe = PKG / "bin" / src.stem
+        exe.parent.mkdir(exist_ok=True)
+        if not force and not _stale(exe, [src, *csrc_h]):
+            built.append(exe)
+            continue
+        cmd = [nvcc(), *ARCH, "-O3", "-std=c++17", "-lineinfo", f"-I{CSRC}", f"-I{INCLUDE}",
+               "-o", str(exe), str(src), "-lcudart"]
+        _run(cmd, verbose)
+        built.append(exe)
     return built
 
 

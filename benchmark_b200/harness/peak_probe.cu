@@ -1,0 +1,366 @@
+// peak_probe -- throughput probes behind the rooflines this library reports.
+//
+// Stands in for the reference's microbenchmarks 1.mma (tcgen05.mma rate),
+// 2.TMEM_LDST (TMEM load/store rate) and the exp/MUFU rate its softmax
+// design assumes, plus a plain HBM copy:
+//
+//   peak_probe [--probe mma|tmem|mufu|hbm|all] [--iters N] [--device N]
+//
+// One CTA per SM.  Each probe prints one line `probe=... value=... unit=...`
+// with the per-SM cycle count behind it.  Operand values do not matter for a
+// rate: shared-memory operands are zero, TMEM operands are whatever the
+// accumulators hold.  Every wait is bounded (ptx.cuh); exit code 1 if one ran
+// out or a CUDA call failed, 2 on bad arguments, 77 without an sm_100 device.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "ptx.cuh"
+
+using namespace b200;
+
+namespace {
+
+constexpr int kSmemProbe = 120 * 1024;  // keeps one CTA (and its 512 TMEM columns) per SM
+
+// tcgen05.mma M=128, N (128 or 256), K=16, bf16 -> fp32, A from shared memory
+// (ts = 0), TMEM (ts = 1) or alternating (ts = 2: shared-A MMAs into one
+// accumulator, TMEM-A MMAs into another, the attention kernel's S/PV mix),
+// issued back to back by one warp.  accs = 2 alternates the accumulator
+// between columns [0, N) and [128, 128 + N) (N = 128 only).
+__global__ void __launch_bounds__(128, 1)
+    mma_probe(int n, int ts, int accs, int iters, unsigned long long* cycles) {
+  extern __shared__ uint8_t raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* a = smem;                         // 128 x 64 bf16, K-major SW128 (16 KiB)
+  uint8_t* b = smem + 16384;                 // 256 x 64 bf16, K-major SW128 (32 KiB)
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 16384 + 32768);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + 16384 + 32768 + 16);
+  for (int i = threadIdx.x; i < (16384 + 32768) / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (warp_id() == 0) {
+    tmem_alloc(slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  if (warp_id() == 0) {
+    // The whole warp runs the loop and one elected lane issues, as the
+    // kernels issue their MMAs.
+    const uint32_t idesc = idesc_bf16_f32(128, n, false, false);
+    const uint64_t da = sdesc_sw128(smem_u32(a), 16, 1024);
+    const uint64_t db = sdesc_sw128(smem_u32(b), 16, 1024);
+    const unsigned long long t0 = clock64();
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t d = tmem + ((accs == 2 && (k & 1)) ? 128u : 0u);
+        if (ts == 1 || (ts == 2 && (k & 1)))
+          mma_ts_warp(d, tmem + 256 + k * 8, db + k * 2, idesc, 1u);
+        else
+          mma_ss_warp(d, da + k * 2, db + k * 2, idesc, 1u);
+      }
+    }
+    mma_commit_warp(bar);
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, 0, 0x51));
+    const unsigned long long t1 = clock64();
+    if (lane_id() == 0) cycles[blockIdx.x] = ok ? t1 - t0 : 0ull;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp_id() == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// tcgen05.mma.cta_group::2 M=256 (128 rows per CTA), N (128 or 256), K=16,
+// both operands from shared memory, issued by the even CTA of each pair.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
+    mma_pair_probe(int n, int iters, unsigned long long* cycles) {
+  extern __shared__ uint8_t raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* a = smem;           // this CTA's 128 x 64 A rows (16 KiB)
+  uint8_t* b = smem + 16384;   // this CTA's N/2 x 64 B rows (up to 16 KiB)
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 32768);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + 32768 + 16);
+  const bool leader = cluster_ctarank() == 0;
+  for (int i = threadIdx.x; i < 32768 / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (warp_id() == 0) {
+    tmem_alloc_pair(slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  if (warp_id() == 0 && leader) {
+    const uint32_t idesc = idesc_bf16_f32(256, n, false, false);
+    const uint64_t da = sdesc_sw128(smem_u32(a), 16, 1024);
+    const uint64_t db = sdesc_sw128(smem_u32(b), 16, 1024);
+    const unsigned long long t0 = clock64();
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mma_ss_pair_warp(tmem, da + k * 2, db + k * 2, idesc, 1u);
+    }
+    if (lane_id() == 0) mma_commit_pair_local(bar);
+    __syncwarp();
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, 0, 0x52));
+    const unsigned long long t1 = clock64();
+    if (lane_id() == 0) cycles[blockIdx.x >> 1] = ok ? t1 - t0 : 0ull;
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp_id() == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+// tcgen05.ld / tcgen05.st 32x32b.x32 by four warps (each its lane quadrant).
+__global__ void __launch_bounds__(128, 1) tmem_probe(int store, int iters,
+                                                     unsigned long long* cycles,
+                                                     uint32_t* sink) {
+  extern __shared__ uint8_t raw[];
+  uint32_t* slot = reinterpret_cast<uint32_t*>(
+      (reinterpret_cast<uintptr_t>(raw) + 15) & ~static_cast<uintptr_t>(15));
+  if (warp_id() == 0) {
+    tmem_alloc(slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot + ((warp_id() * 32u) << 16);
+  uint32_t v[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) v[e] = threadIdx.x + e;
+  uint32_t acc = 0;
+  __syncthreads();
+  const unsigned long long t0 = clock64();
+  for (int it = 0; it < iters; ++it) {
+    const uint32_t col = static_cast<uint32_t>((it & 15) * 32);
+    if (store) {
+      tmem_st32(tmem + col, v);
+    } else {
+      tmem_ld32(tmem + col, v);
+      tmem_wait_ld(v);
+      acc ^= v[it & 31];
+    }
+  }
+  if (store) tmem_wait_st();
+  __syncthreads();
+  const unsigned long long t1 = clock64();
+  if (threadIdx.x == 0) cycles[blockIdx.x] = t1 - t0;
+  sink[blockIdx.x * blockDim.x + threadIdx.x] = acc;
+  tc_fence_before();
+  __syncthreads();
+  if (warp_id() == 0) {
+    tc_fence_after();
+    tmem_dealloc(*slot, 512);
+  }
+}
+
+// MUFU ex2.approx.ftz.f32: eight independent chains per thread, 8 warps.
+__global__ void mufu_probe(int iters, unsigned long long* cycles, float* sink) {
+  float x[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = -1e-3f * (threadIdx.x + i);
+  __syncthreads();
+  const unsigned long long t0 = clock64();
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) asm volatile("ex2.approx.ftz.f32 %0, %0;" : "+f"(x[i]));
+  }
+  __syncthreads();
+  const unsigned long long t1 = clock64();
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s += x[i];
+  sink[blockIdx.x * blockDim.x + threadIdx.x] = s;
+  if (threadIdx.x == 0) cycles[blockIdx.x] = t1 - t0;
+}
+
+__global__ void copy_probe(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    dst[i] = src[i];
+}
+
+double mean_cycles(const unsigned long long* d, int n) {
+  unsigned long long h[1024];
+  cudaMemcpy(h, d, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+  double s = 0;
+  int k = 0;
+  for (int i = 0; i < n; ++i)
+    if (h[i]) {
+      s += static_cast<double>(h[i]);
+      ++k;
+    }
+  return k ? s / k : 0.0;
+}
+
+bool status_ok() {
+  uint32_t st = 0;
+  cudaMemcpyFromSymbol(&st, g_status, sizeof(st));
+  if (st != 0) {
+    std::fprintf(stderr, "device wait timed out (status 0x%08x)\n", st);
+    const uint32_t zero = 0;
+    cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
+    return false;
+  }
+  return cudaGetLastError() == cudaSuccess;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  std::string probe = "all";
+  int iters = 4096, device = 0;
+  for (int i = 1; i < argc; ++i) {
+    const std::string f = argv[i];
+    auto next = [&]() -> const char* {
+      if (i + 1 >= argc) std::exit(2);
+      return argv[++i];
+    };
+    if (f == "--help") {
+      std::printf("peak_probe [--probe mma|tmem|mufu|hbm|all] [--iters N] [--device N]\n");
+      return 0;
+    } else if (f == "--probe") probe = next();
+    else if (f == "--iters") iters = std::atoi(next());
+    else if (f == "--device") device = std::atoi(next());
+    else {
+      std::fprintf(stderr, "unknown argument %s\n", f.c_str());
+      return 2;
+    }
+  }
+  if (iters < 16 || iters > (1 << 20) ||
+      (probe != "mma" && probe != "tmem" && probe != "mufu" && probe != "hbm" && probe != "all")) {
+    std::fprintf(stderr, "invalid arguments (see --help)\n");
+    return 2;
+  }
+  cudaDeviceProp prop{};
+  if (cudaSetDevice(device) != cudaSuccess ||
+      cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major < 10) {
+    std::fprintf(stderr, "no sm_100 device %d\n", device);
+    return 77;
+  }
+  const int sms = prop.multiProcessorCount;
+  int clock_khz = 0;
+  cudaDeviceGetAttribute(&clock_khz, cudaDevAttrClockRate, device);
+  unsigned long long* cyc = nullptr;
+  uint32_t* sink = nullptr;
+  cudaMalloc(&cyc, 1024 * sizeof(unsigned long long));
+  cudaMalloc(&sink, 1024 * 1024 * sizeof(uint32_t));
+  cudaFuncSetAttribute(mma_probe, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemProbe);
+  cudaFuncSetAttribute(tmem_probe, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemProbe);
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  int rc = 0;
+  auto timed = [&](auto launch) {
+    launch();  // warm-up
+    cudaDeviceSynchronize();
+    cudaMemset(cyc, 0, 1024 * sizeof(unsigned long long));
+    cudaEventRecord(e0);
+    launch();
+    cudaEventRecord(e1);
+    cudaEventSynchronize(e1);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    if (!status_ok()) rc = 1;
+    return static_cast<double>(ms);
+  };
+  if (probe == "mma" || probe == "all") {
+    // {N, A source, accumulators}
+    const int shapes[6][3] = {{256, 0, 1}, {128, 0, 1}, {128, 1, 1},
+                              {128, 0, 2}, {128, 1, 2}, {128, 2, 2}};
+    const char* src_name[3] = {"ss", "ts", "ss_ts"};
+    for (const auto& sh : shapes) {
+      const int n = sh[0], ts = sh[1], accs = sh[2];
+      const double ms = timed([&] {
+        mma_probe<<<sms, 128, kSmemProbe>>>(n, ts, accs, iters, cyc);
+      });
+      const double per_mma = mean_cycles(cyc, sms) / (4.0 * iters);
+      const double flops = 2.0 * 128 * n * 16 * 4.0 * iters * sms;
+      std::printf("probe=mma_m128_n%d_%s_%dacc cycles_per_mma=%.2f value=%.1f unit=TFLOP/s "
+                  "ms=%.4f\n", n, src_name[ts], accs, per_mma, flops / (ms * 1e-3) / 1e12, ms);
+    }
+  }
+  if (probe == "mma" || probe == "all") {
+    cudaFuncSetAttribute(mma_pair_probe, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kSmemProbe);
+    for (int n : {128, 256}) {
+      const int pairs = sms / 2;
+      const double ms = timed([&] {
+        mma_pair_probe<<<2 * pairs, 128, kSmemProbe>>>(n, iters, cyc);
+      });
+      const double per_mma = mean_cycles(cyc, pairs) / (4.0 * iters);
+      const double flops = 2.0 * 256 * n * 16 * 4.0 * iters * pairs;
+      std::printf("probe=mma_pair_m256_n%d_ss cycles_per_mma=%.2f value=%.1f unit=TFLOP/s "
+                  "ms=%.4f\n", n, per_mma, flops / (ms * 1e-3) / 1e12, ms);
+    }
+  }
+  if (probe == "tmem" || probe == "all") {
+    for (int store = 0; store < 2; ++store) {
+      const double ms = timed([&] {
+        tmem_probe<<<sms, 128, kSmemProbe>>>(store, iters, cyc, sink);
+      });
+      const double c = mean_cycles(cyc, sms);
+      const double bytes_per_sm = 128.0 * 32 * 4 * iters;
+      std::printf("probe=tmem_%s_32x32b_x32 bytes_per_cycle_per_sm=%.1f value=%.1f unit=TB/s "
+                  "ms=%.4f\n", store ? "st" : "ld", bytes_per_sm / c,
+                  bytes_per_sm * sms / (ms * 1e-3) / 1e12, ms);
+    }
+  }
+  if (probe == "mufu" || probe == "all") {
+    const double ms = timed([&] {
+      mufu_probe<<<sms, 256>>>(iters, cyc, reinterpret_cast<float*>(sink));
+    });
+    const double c = mean_cycles(cyc, sms);
+    const double ops = 256.0 * 8 * iters;
+    std::printf("probe=mufu_ex2_f32 lanes_per_cycle_per_sm=%.2f value=%.1f unit=Gop/s ms=%.4f\n",
+                ops / c, ops * sms / (ms * 1e-3) / 1e9, ms);
+  }
+  if (probe == "hbm" || probe == "all") {
+    const size_t bytes = static_cast<size_t>(1) << 30;
+    void *src = nullptr, *dst = nullptr;
+    if (cudaMalloc(&src, bytes) != cudaSuccess || cudaMalloc(&dst, bytes) != cudaSuccess) {
+      std::fprintf(stderr, "hbm probe: allocation failed\n");
+      rc = 1;
+    } else {
+      cudaMemset(src, 1, bytes);
+      const size_t n = bytes / 16;
+      const double ms = timed([&] {
+        copy_probe<<<sms * 8, 512>>>(static_cast<const uint4*>(src), static_cast<uint4*>(dst),
+                                     n);
+      });
+      std::printf("probe=hbm_copy_1GiB value=%.1f unit=GB/s (read+write) ms=%.4f\n",
+                  2.0 * bytes / (ms * 1e-3) / 1e9, ms);
+    }
+    cudaFree(src);
+    cudaFree(dst);
+  }
+  std::printf("device=\"%s\" sms=%d clock_khz=%d\n", prop.name, sms, clock_khz);
+  cudaFree(cyc);
+  cudaFree(sink);
+  return rc;
+}

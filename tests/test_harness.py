@@ -12,6 +12,7 @@ BIN = Path(__file__).resolve().parents[1] / "benchmark_b200" / "bin"
 ATTN = BIN / "attention_bench"
 GEMM = BIN / "gemm_bench"
 CUBLAS = BIN / "cublas_bench"
+PROBE = BIN / "peak_probe"
 
 
 def _run(exe, *args, timeout=600):
@@ -20,7 +21,7 @@ def _run(exe, *args, timeout=600):
     return subprocess.run([str(exe), *args], capture_output=True, text=True, timeout=timeout)
 
 
-@pytest.mark.parametrize("exe", [ATTN, GEMM, CUBLAS])
+@pytest.mark.parametrize("exe", [ATTN, GEMM, CUBLAS, PROBE])
 def test_help_exits_zero(exe):
     r = _run(exe, "--help")
     assert r.returncode == 0 and "--" in r.stdout
@@ -93,3 +94,28 @@ def test_cublas_bench_modes_run(mode):
     csv_line = [ln for ln in r.stdout.splitlines() if ln.startswith("csv,")]
     assert len(csv_line) == 1 and csv_line[0].split(",")[1] == mode
     assert float(csv_line[0].split(",")[8]) > 0
+
+
+def test_peak_probe_bad_arguments_exit_two():
+    assert _run(PROBE, "--probe", "fp8").returncode == 2
+    assert _run(PROBE, "--iters", "1").returncode == 2
+
+
+@pytest.mark.gpu
+def test_peak_probe_all_runs_with_plausible_rates():
+    r = _run(PROBE, "--probe", "all", "--iters", "2048")
+    assert r.returncode == 0, r.stdout + r.stderr
+    vals = {}
+    for ln in r.stdout.splitlines():
+        if ln.startswith("probe="):
+            kv = dict(x.split("=", 1) for x in ln.split() if "=" in x)
+            vals[kv["probe"]] = float(kv["value"])
+    assert set(vals) == {"mma_m128_n256_ss_1acc", "mma_m128_n128_ss_1acc",
+                         "mma_m128_n128_ts_1acc", "mma_m128_n128_ss_2acc",
+                         "mma_m128_n128_ts_2acc", "mma_m128_n128_ss_ts_2acc",
+                         "mma_pair_m256_n128_ss", "mma_pair_m256_n256_ss",
+                         "tmem_ld_32x32b_x32", "tmem_st_32x32b_x32", "mufu_ex2_f32",
+                         "hbm_copy_1GiB"}
+    assert vals["mma_m128_n256_ss_1acc"] > 500  # TFLOP/s
+    assert vals["hbm_copy_1GiB"] > 1000        # GB/s
+    assert all(v > 0 for v in vals.values())
