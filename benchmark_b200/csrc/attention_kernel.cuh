@@ -39,8 +39,8 @@
 //   issue order.
 //
 // Softmax per tile: a thread reads 32 scores of each of its two rows
-// (16x256b TMEM loads), the row max is completed by two shuffles, and the
-// running max m is kept in log2 units.  O and the row sums are rescaled only
+// (16x256b TMEM loads); where a row max is needed it is completed by two
+// shuffles, and the running max m is kept in log2 units.  O and the row sums are rescaled only
 // when a block raises m by more than kRescaleLog2 (otherwise P values up to
 // 2^kRescaleLog2 accumulate unscaled: exact in fp32, O / l unchanged), after
 // PV(t-1) has completed.  P is stored with 16x128b stores, whose column
@@ -63,9 +63,23 @@ constexpr int kEpiWarp0 = 8;
 constexpr int kTmaWarp = 12;   // Q and K loads
 constexpr int kMmaWarp = 13;
 constexpr int kTmaVWarp = 14;  // V loads
-constexpr int kThreads = 480;
+constexpr int kThreads = 512;  // warp 15 only completes warpgroup 3
+// Registers per thread after the split: softmax warpgroups 0-1 grow, the
+// epilogue warpgroup 2 and the producer/issuer warpgroup 3 shrink; the sum is
+// the pool the block launches with (512 threads x 128).
+constexpr int kLaunchRegs = 65536 / kThreads;
+constexpr int kSoftmaxRegs = 184;
+constexpr int kEpiRegs = 56;
+constexpr int kCtlRegs = 88;
+static_assert(8 * 32 * kSoftmaxRegs + 4 * 32 * kEpiRegs + 4 * 32 * kCtlRegs ==
+                  kThreads * kLaunchRegs,
+              "register split must use exactly the launch pool");
+static_assert(kSoftmaxRegs % 8 == 0 && kEpiRegs % 8 == 0 && kCtlRegs % 8 == 0 &&
+                  kEpiRegs >= 24 && kCtlRegs >= 24 && kSoftmaxRegs <= 256,
+              "setmaxnreg counts");
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
+constexpr float kRescaleP = 256.0f;  // 2^kRescaleLog2
 constexpr int kSBufs = 3;  // S buffers in TMEM (P overwrites its S buffer)
 constexpr int kBarEpilogue = 1;  // named barrier: warps 8-11
 
@@ -255,43 +269,6 @@ __device__ __forceinline__ void p_rows(const float* s, float sc, float nm_a, flo
   }
 }
 
-// p_rows for an unmasked block against a running max that may be stale:
-// also reduces the max of x over the block per row (mx_a, mx_b), on the ALU
-// pipe while the exponentials occupy MUFU.
-template <int kEmu>
-__device__ __forceinline__ void p_rows_max(const float* s, float sc, float nm_a, float nm_b,
-                                           uint64_t& rs_a, uint64_t& rs_b, uint32_t (&pk)[16],
-                                           float& mx_a, float& mx_b) {
-  const uint64_t sc2 = f2_pack(sc, sc);
-  const uint64_t na2 = f2_pack(nm_a, nm_a);
-  const uint64_t nb2 = f2_pack(nm_b, nm_b);
-#pragma unroll
-  for (int g = 0; g < 8; ++g) {
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      const uint64_t x2 = f2_fma(f2_pack(s[4 * g + 2 * rr], s[4 * g + 2 * rr + 1]), sc2,
-                                 rr ? nb2 : na2);
-      float x0, x1, p0, p1;
-      f2_unpack(x2, x0, x1);
-      if (rr)
-        mx_b = fmax3(mx_b, x0, x1);
-      else
-        mx_a = fmax3(mx_a, x0, x1);
-      if (((2 * g + rr) & 7) < kEmu) {
-        exp2_fma_x2(x0, x1, p0, p1);
-      } else {
-        p0 = ex2_approx(x0);
-        p1 = ex2_approx(x1);
-      }
-      if (rr)
-        rs_b = f2_add(rs_b, f2_pack(p0, p1));
-      else
-        rs_a = f2_add(rs_a, f2_pack(p0, p1));
-      pk[2 * g + rr] = pack_bf16x2(p0, p1);
-    }
-  }
-}
-
 template <int D, int kEmu, bool kTrace = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_fwd_kernel(const __grid_constant__ CUtensorMap q_map,
@@ -371,218 +348,224 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const bool trace_cta = kTrace && static_cast<int>(blockIdx.x) == p.trace_cta;
-
-  if (warp == kTmaWarp || warp == kTmaVWarp) {
-    // ================= TMA producers (Q + K, and V) =================
-    if (lane == 0) {
-      const bool is_k = warp == kTmaWarp;
-      Tracer<kTrace> tr(p, 0, trace_cta && is_k);
-      const uint64_t pol_q = l2_policy_evict_first();
-      const uint64_t pol_kv = l2_policy_evict_last();
-      int t = 0, li = 0, issued = 0, q_issued = -1;
-      bool ok = true;
-      for (int r = 0; r < rounds && ok; ++r) {
-        const int k = item_index(p, r);
-        if (k >= p.n_items) continue;
-        const Item it = decode_item(p, k);
-        const int qb = li & 1;
-        const uint32_t qpar = static_cast<uint32_t>(li >> 1) & 1u;
-        ++li;
-        if (is_k) {
-          // Q(li) reuses the buffer the epilogue of item li-2 staged O in.
-          ok = mbar_wait(&q_empty[qb], qpar ^ 1u, kSiteQEmpty);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&q_full[qb], C::kTileBytes);
-          for (int h = 0; h < C::kBoxes; ++h)
-            tma_load_3d(q_buf + qb * C::kTileBytes + h * C::kBoxBytes, &q_map, &q_full[qb],
-                        h * 64, it.row0, it.zq, pol_q);
-          q_issued = li - 1;
-          tr(kEvTmaQ, qb, li - 1);
-        }
-        for (int j = 0; j < it.n; ++j, ++t) {
+  // Each warpgroup moves its register budget first, inside its own branch,
+  // so the compiler sizes each role's code to that role's budget.
+  if (warp >= static_cast<uint32_t>(kTmaWarp)) {
+    // Warpgroup 3: producers and MMA issuer (warp 15 only completes the group).
+    setmaxnreg_dec<kCtlRegs>();
+    if (warp == kTmaWarp || warp == kTmaVWarp) {
+      // ================= TMA producers (Q + K, and V) =================
+      if (lane == 0) {
+        const bool is_k = warp == kTmaWarp;
+        Tracer<kTrace> tr(p, 0, trace_cta && is_k);
+        const uint64_t pol_q = l2_policy_evict_first();
+        const uint64_t pol_kv = l2_policy_evict_last();
+        int t = 0, li = 0, issued = 0, q_issued = -1;
+        bool ok = true;
+        for (int r = 0; r < rounds && ok; ++r) {
+          const int k = item_index(p, r);
+          if (k >= p.n_items) continue;
+          const Item it = decode_item(p, k);
+          const int qb = li & 1;
+          const uint32_t qpar = static_cast<uint32_t>(li >> 1) & 1u;
+          ++li;
           if (is_k) {
-            const int ks = t % C::kKStages;
-            ok = mbar_wait(&k_empty[ks], (static_cast<uint32_t>(t / C::kKStages) & 1u) ^ 1u,
-                           kSiteKEmpty);
+            // Q(li) reuses the buffer the epilogue of item li-2 staged O in.
+            ok = mbar_wait(&q_empty[qb], qpar ^ 1u, kSiteQEmpty, kDefaultWaitLimitNs, 20000u);
             if (!ok) break;
-            tr(kEvTmaK, 0, t);
-            mbar_arrive_expect_tx(&k_full[ks], C::kTileBytes);
+            mbar_arrive_expect_tx(&q_full[qb], C::kTileBytes);
             for (int h = 0; h < C::kBoxes; ++h)
-              tma_load_3d(k_buf + ks * C::kTileBytes + h * C::kBoxBytes, &k_map, &k_full[ks],
-                          h * 64, j * kBN, it.zkv, pol_kv);
-          } else {
-            const int vs = t % C::kVStages;
-            ok = mbar_wait(&v_empty[vs], (static_cast<uint32_t>(t / C::kVStages) & 1u) ^ 1u,
-                           kSiteVEmpty);
-            if (!ok) break;
-            mbar_arrive_expect_tx(&v_full[vs], C::kTileBytes);
-            for (int h = 0; h < C::kBoxes; ++h)
-              tma_load_3d(v_buf + vs * C::kTileBytes + h * C::kBoxBytes, &v_map, &v_full[vs],
-                          h * 64, j * kBN, it.zkv, pol_kv);
+              tma_load_3d(q_buf + qb * C::kTileBytes + h * C::kBoxBytes, &q_map, &q_full[qb],
+                          h * 64, it.row0, it.zq, pol_q);
+            q_issued = li - 1;
+            tr(kEvTmaQ, qb, li - 1);
           }
-          issued = t + 1;
+          for (int j = 0; j < it.n; ++j, ++t) {
+            if (is_k) {
+              const int ks = t % C::kKStages;
+              ok = mbar_wait(&k_empty[ks], (static_cast<uint32_t>(t / C::kKStages) & 1u) ^ 1u,
+                             kSiteKEmpty, kDefaultWaitLimitNs, 20000u);
+              if (!ok) break;
+              tr(kEvTmaK, 0, t);
+              mbar_arrive_expect_tx(&k_full[ks], C::kTileBytes);
+              for (int h = 0; h < C::kBoxes; ++h)
+                tma_load_3d(k_buf + ks * C::kTileBytes + h * C::kBoxBytes, &k_map, &k_full[ks],
+                            h * 64, j * kBN, it.zkv, pol_kv);
+            } else {
+              const int vs = t % C::kVStages;
+              ok = mbar_wait(&v_empty[vs], (static_cast<uint32_t>(t / C::kVStages) & 1u) ^ 1u,
+                             kSiteVEmpty, kDefaultWaitLimitNs, 20000u);
+              if (!ok) break;
+              mbar_arrive_expect_tx(&v_full[vs], C::kTileBytes);
+              for (int h = 0; h < C::kBoxes; ++h)
+                tma_load_3d(v_buf + vs * C::kTileBytes + h * C::kBoxBytes, &v_map, &v_full[vs],
+                            h * 64, j * kBN, it.zkv, pol_kv);
+            }
+            issued = t + 1;
+          }
+        }
+        if (!ok) {
+          // Unwinding: let every copy already issued land before the CTA exits.
+          if (is_k) {
+            if (q_issued >= 0)
+              drain_wait(&q_full[q_issued & 1], static_cast<uint32_t>(q_issued >> 1) & 1u);
+            for (int i = max(0, issued - C::kKStages); i < issued; ++i)
+              drain_wait(&k_full[i % C::kKStages], static_cast<uint32_t>(i / C::kKStages) & 1u);
+          } else {
+            for (int i = max(0, issued - C::kVStages); i < issued; ++i)
+              drain_wait(&v_full[i % C::kVStages], static_cast<uint32_t>(i / C::kVStages) & 1u);
+          }
         }
       }
-      if (!ok) {
-        // Unwinding: let every copy already issued land before the CTA exits.
-        if (is_k) {
-          if (q_issued >= 0)
-            drain_wait(&q_full[q_issued & 1], static_cast<uint32_t>(q_issued >> 1) & 1u);
-          for (int i = max(0, issued - C::kKStages); i < issued; ++i)
-            drain_wait(&k_full[i % C::kKStages], static_cast<uint32_t>(i / C::kKStages) & 1u);
-        } else {
-          for (int i = max(0, issued - C::kVStages); i < issued; ++i)
-            drain_wait(&v_full[i % C::kVStages], static_cast<uint32_t>(i / C::kVStages) & 1u);
-        }
-      }
-    }
-    __syncwarp();
-  } else if (warp == kMmaWarp) {
-    // ================= MMA issuer =================
-    // The whole warp runs this loop (operands stay warp-uniform); one elected
-    // lane issues each MMA and commit.
-    {
-      Tracer<kTrace> tr(p, 1, trace_cta && lane == 0);
-      const uint32_t q_addr = smem_u32(q_buf);
-      const uint32_t k_addr = smem_u32(k_buf);
-      const uint32_t v_addr = smem_u32(v_buf);
-      // Descriptors are built once; a K step, ring stage or Q buffer only
-      // moves the start address, i.e. adds (byte offset >> 4) to the low
-      // field (shared addresses stay below 2^18: the 14-bit field never carries).
-      const uint64_t dq0 = sdesc_sw128(q_addr, 16, 1024);
-      const uint64_t dk0 = sdesc_sw128(k_addr, 16, 1024);
-      const uint64_t dv0 = sdesc_sw128(v_addr, C::kBoxBytes, 1024);
-      constexpr uint32_t kTile16 = C::kTileBytes >> 4, kBox16 = C::kBoxBytes >> 4;
-      const uint32_t tO = tmem_base + C::kColO;
-      // Filler for unused slots of the grouped waits.
-      const uint32_t dn_a = smem_u32(done), dn_p = 0;
-      auto bar = [](uint64_t* b_) { return smem_u32(b_); };
-      auto kpar = [](int t_) { return static_cast<uint32_t>(t_ / C::kKStages) & 1u; };
-      auto vpar = [](int t_) { return static_cast<uint32_t>(t_ / C::kVStages) & 1u; };
-      auto wait3 = [&](uint32_t a0, uint32_t p0, uint32_t a1, uint32_t p1, uint32_t a2,
-                       uint32_t p2, uint32_t site) -> bool {
-        tr(kEvMmaWait, site, 0);
-        if (!__all_sync(0xffffffffu, mbar_wait3(a0, p0, a1, p1, a2, p2, site))) return false;
-        tc_fence_after();
-        tr(kEvMmaGo, site, 0);
-        return true;
-      };
-      // S(t) = Q[qb] K(t)^T into S buffer t % kSBufs.
-      auto issue_s = [&](int t_, int qb) {
-        tr(kEvMmaS, qb, t_);
-        const uint64_t dq = dq0 + qb * kTile16;
-        const uint64_t dk = dk0 + (t_ % C::kKStages) * kTile16;
-        const uint32_t ts = tmem_base + static_cast<uint32_t>((t_ % kSBufs) * 128);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kBox16 + (kk & 3) * 2;
-          mma_ss_warp(ts, dq + off, dk + off, C::kIdescS, kk > 0 ? 1u : 0u);
-        }
-        mma_commit_warp(&k_empty[t_ % C::kKStages]);
-        mma_commit_warp(&s_ready[t_ % kSBufs]);
-      };
-      // O (+)= P(t)[keys 64*half ...] V(t)[keys 64*half ...]
-      auto issue_pv_half = [&](int t_, bool first, int half) {
-        tr(half ? kEvMmaPvHi : kEvMmaPvLo, 0, t_);
-        const uint64_t dv = dv0 + (t_ % C::kVStages) * kTile16;
-        const uint32_t tp = tmem_base + static_cast<uint32_t>((t_ % kSBufs) * 128);
-#pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-          const int kk = half * 4 + k4;
-          mma_ts_warp(tO, tp + kk * 8, dv + kk * (2048 >> 4), C::kIdescO,
-                      (!first || kk > 0) ? 1u : 0u);
-        }
-      };
-      // Next valid round after r (rounds if none).
-      auto next_round = [&](int r) {
-        for (++r; r < rounds; ++r)
-          if (item_index(p, r) < p.n_items) break;
-        return r;
-      };
+      __syncwarp();
+    } else if (warp == kMmaWarp) {
+      // ================= MMA issuer =================
+      // The whole warp runs this loop (operands stay warp-uniform); one elected
+      // lane issues each MMA and commit.
+      {
+        Tracer<kTrace> tr(p, 1, trace_cta && lane == 0);
+        const uint32_t q_addr = smem_u32(q_buf);
+        const uint32_t k_addr = smem_u32(k_buf);
+        const uint32_t v_addr = smem_u32(v_buf);
+        // Descriptors are built once; a K step, ring stage or Q buffer only
+        // moves the start address, i.e. adds (byte offset >> 4) to the low
+        // field (shared addresses stay below 2^18: the 14-bit field never carries).
+        const uint64_t dq0 = sdesc_sw128(q_addr, 16, 1024);
+        const uint64_t dk0 = sdesc_sw128(k_addr, 16, 1024);
+        const uint64_t dv0 = sdesc_sw128(v_addr, C::kBoxBytes, 1024);
+        constexpr uint32_t kTile16 = C::kTileBytes >> 4, kBox16 = C::kBoxBytes >> 4;
+        const uint32_t tO = tmem_base + C::kColO;
+        // Filler for unused slots of the grouped waits.
+        const uint32_t dn_a = smem_u32(done), dn_p = 0;
+        auto bar = [](uint64_t* b_) { return smem_u32(b_); };
+        auto kpar = [](int t_) { return static_cast<uint32_t>(t_ / C::kKStages) & 1u; };
+        auto vpar = [](int t_) { return static_cast<uint32_t>(t_ / C::kVStages) & 1u; };
+        auto wait3 = [&](uint32_t a0, uint32_t p0, uint32_t a1, uint32_t p1, uint32_t a2,
+                         uint32_t p2, uint32_t site) -> bool {
+          tr(kEvMmaWait, site, 0);
+          if (!__all_sync(0xffffffffu, mbar_wait3(a0, p0, a1, p1, a2, p2, site))) return false;
+          tc_fence_after();
+          tr(kEvMmaGo, site, 0);
+          return true;
+        };
+        // S(t) = Q[qb] K(t)^T into S buffer t % kSBufs.
+        auto issue_s = [&](int t_, int qb) {
+          tr(kEvMmaS, qb, t_);
+          const uint64_t dq = dq0 + qb * kTile16;
+          const uint64_t dk = dk0 + (t_ % C::kKStages) * kTile16;
+          const uint32_t ts = tmem_base + static_cast<uint32_t>((t_ % kSBufs) * 128);
+  #pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kBox16 + (kk & 3) * 2;
+            mma_ss_warp(ts, dq + off, dk + off, C::kIdescS, kk > 0 ? 1u : 0u);
+          }
+          mma_commit_warp(&k_empty[t_ % C::kKStages]);
+          mma_commit_warp(&s_ready[t_ % kSBufs]);
+        };
+        // O (+)= P(t)[keys 64*half ...] V(t)[keys 64*half ...]
+        auto issue_pv_half = [&](int t_, bool first, int half) {
+          tr(half ? kEvMmaPvHi : kEvMmaPvLo, 0, t_);
+          const uint64_t dv = dv0 + (t_ % C::kVStages) * kTile16;
+          const uint32_t tp = tmem_base + static_cast<uint32_t>((t_ % kSBufs) * 128);
+  #pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const int kk = half * 4 + k4;
+            mma_ts_warp(tO, tp + kk * 8, dv + kk * (2048 >> 4), C::kIdescO,
+                        (!first || kk > 0) ? 1u : 0u);
+          }
+        };
+        // Next valid round after r (rounds if none).
+        auto next_round = [&](int r) {
+          for (++r; r < rounds; ++r)
+            if (item_index(p, r) < p.n_items) break;
+          return r;
+        };
 
-      // S cursor: the next S to issue, up to kSBufs - 1 tiles ahead of the
-      // PV cursor and never beyond the item after the PV cursor's (the Q of
-      // a later item waits for an epilogue that waits for this thread).
-      int s_r = next_round(-1), s_li = 0, s_j = 0, s_t = 0;
-      Item s_it{};
-      auto s_settle = [&]() {  // move past items without K/V tiles
-        while (s_r < rounds) {
-          s_it = decode_item(p, item_index(p, s_r));
-          if (s_it.n > 0) break;
-          s_r = next_round(s_r);
-          ++s_li;
-        }
-      };
-      s_settle();
-      auto issue_s_upto = [&](int limit_t, int max_li) -> bool {
-        while (s_r < rounds && s_t <= limit_t && s_li <= max_li) {
-          const int qb = s_li & 1;
-          if (s_j == 0 &&
-              !wait3(bar(&q_full[qb]), static_cast<uint32_t>(s_li >> 1) & 1u, dn_a, dn_p, dn_a,
-                     dn_p, kSiteQFull))
-            return false;
-          if (!wait3(bar(&k_full[s_t % C::kKStages]), kpar(s_t), dn_a, dn_p, dn_a, dn_p,
-                     kSiteKFull))
-            return false;
-          issue_s(s_t, qb);
-          ++s_t;
-          if (++s_j == s_it.n) {
-            s_j = 0;
+        // S cursor: the next S to issue, up to kSBufs - 1 tiles ahead of the
+        // PV cursor and never beyond the item after the PV cursor's (the Q of
+        // a later item waits for an epilogue that waits for this thread).
+        int s_r = next_round(-1), s_li = 0, s_j = 0, s_t = 0;
+        Item s_it{};
+        auto s_settle = [&]() {  // move past items without K/V tiles
+          while (s_r < rounds) {
+            s_it = decode_item(p, item_index(p, s_r));
+            if (s_it.n > 0) break;
             s_r = next_round(s_r);
             ++s_li;
-            s_settle();
           }
-        }
-        return true;
-      };
+        };
+        s_settle();
+        auto issue_s_upto = [&](int limit_t, int max_li) -> bool {
+          while (s_r < rounds && s_t <= limit_t && s_li <= max_li) {
+            const int qb = s_li & 1;
+            if (s_j == 0 &&
+                !wait3(bar(&q_full[qb]), static_cast<uint32_t>(s_li >> 1) & 1u, dn_a, dn_p, dn_a,
+                       dn_p, kSiteQFull))
+              return false;
+            if (!wait3(bar(&k_full[s_t % C::kKStages]), kpar(s_t), dn_a, dn_p, dn_a, dn_p,
+                       kSiteKFull))
+              return false;
+            issue_s(s_t, qb);
+            ++s_t;
+            if (++s_j == s_it.n) {
+              s_j = 0;
+              s_r = next_round(s_r);
+              ++s_li;
+              s_settle();
+            }
+          }
+          return true;
+        };
 
-      // PV cursor.
-      int t = 0, li = 0;
-      bool ok = true;
-      for (int r = next_round(-1); r < rounds && ok; r = next_round(r), ++li) {
-        const Item it = decode_item(p, item_index(p, r));
-        const uint32_t oe_par = (static_cast<uint32_t>(li) & 1u) ^ 1u;  // epilogue of li-1
-        if (it.n == 0) {
-          // No K/V tiles: O stays unwritten (the epilogue stores zeros in Q's
-          // buffer, so Q(li) must have landed first).
-          ok = wait3(bar(&q_full[li & 1]), static_cast<uint32_t>(li >> 1) & 1u, bar(o_empty),
-                     oe_par, dn_a, dn_p, kSiteQFull);
+        // PV cursor.
+        int t = 0, li = 0;
+        bool ok = true;
+        for (int r = next_round(-1); r < rounds && ok; r = next_round(r), ++li) {
+          const Item it = decode_item(p, item_index(p, r));
+          const uint32_t oe_par = (static_cast<uint32_t>(li) & 1u) ^ 1u;  // epilogue of li-1
+          if (it.n == 0) {
+            // No K/V tiles: O stays unwritten (the epilogue stores zeros in Q's
+            // buffer, so Q(li) must have landed first).
+            ok = wait3(bar(&q_full[li & 1]), static_cast<uint32_t>(li >> 1) & 1u, bar(o_empty),
+                       oe_par, dn_a, dn_p, kSiteQFull);
+            if (!ok) break;
+            mma_commit_warp(o_full);
+            continue;
+          }
+          for (int j = 0; j < it.n && ok; ++j) {
+            const int tt = t + j;
+            const uint32_t tpar = static_cast<uint32_t>(tt / kSBufs) & 1u;
+            ok = issue_s_upto(tt + kSBufs - 1, li + 1);
+            if (!ok) break;
+            if (j == 0) {
+              // O is free once the epilogue of item li-1 has read it.
+              ok = wait3(bar(o_empty), oe_par, dn_a, dn_p, dn_a, dn_p, kSiteOEmpty);
+              if (!ok) break;
+            }
+            // One grouped wait per PV: polls cost a few hundred cycles each,
+            // and S(t+2), issued just before, keeps the tensor pipe busy
+            // meanwhile.
+            ok = wait3(bar(&v_full[tt % C::kVStages]), vpar(tt), bar(&p_ready[tt % kSBufs]), tpar,
+                       dn_a, dn_p, kSitePReady);
+            if (!ok) break;
+            issue_pv_half(tt, j == 0, 0);
+            issue_pv_half(tt, j == 0, 1);
+            mma_commit_warp(&v_empty[tt % C::kVStages]);
+            mma_commit_warp(pv_done);
+          }
           if (!ok) break;
           mma_commit_warp(o_full);
-          continue;
+          t += it.n;
         }
-        for (int j = 0; j < it.n && ok; ++j) {
-          const int tt = t + j;
-          const uint32_t tpar = static_cast<uint32_t>(tt / kSBufs) & 1u;
-          ok = issue_s_upto(tt + kSBufs - 1, li + 1);
-          if (!ok) break;
-          if (j == 0) {
-            // O is free once the epilogue of item li-1 has read it.
-            ok = wait3(bar(o_empty), oe_par, dn_a, dn_p, dn_a, dn_p, kSiteOEmpty);
-            if (!ok) break;
-          }
-          // One grouped wait per PV: polls cost a few hundred cycles each,
-          // and S(t+2), issued just before, keeps the tensor pipe busy
-          // meanwhile.
-          ok = wait3(bar(&v_full[tt % C::kVStages]), vpar(tt), bar(&p_ready[tt % kSBufs]), tpar,
-                     dn_a, dn_p, kSitePReady);
-          if (!ok) break;
-          issue_pv_half(tt, j == 0, 0);
-          issue_pv_half(tt, j == 0, 1);
-          mma_commit_warp(&v_empty[tt % C::kVStages]);
-          mma_commit_warp(pv_done);
-        }
-        if (!ok) break;
-        mma_commit_warp(o_full);
-        t += it.n;
+        // Every MMA issued above has completed once this commit lands.
+        mma_commit_warp(drain);
+        drain_wait(drain, 0);
+        tr(kEvMmaEnd, 0, t);
       }
-      // Every MMA issued above has completed once this commit lands.
-      mma_commit_warp(drain);
-      drain_wait(drain, 0);
-      tr(kEvMmaEnd, 0, t);
+      __syncwarp();
     }
-    __syncwarp();
   } else if (warp < static_cast<uint32_t>(kEpiWarp0)) {
+    setmaxnreg_inc<kSoftmaxRegs>();
     // ================= softmax (warps 0-7) =================
     // Warp w owns 16 rows: TMEM lanes 32*(w%4) + 16*(w/4) + [0,16).  Thread
     // t of the warp holds rows t/4 and t/4+8 and, of every 8 keys, the pair
@@ -625,6 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the P stores and the bookkeeping.
       uint32_t sr[64];
       bool have_s = false;
+      bool all_finite = false;  // every row of this warp has a finite running max
 #pragma unroll 1
       for (int j = 0; j < it.n; ++j) {
         const int tt = t + j;
@@ -645,16 +629,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kbase = j * kBN;
         const bool masked = kbase + kBN > it.min_lim;  // uniform across the tile
         float f_a = 1.0f, f_b = 1.0f;
-        bool rescale = false;
+        bool rescale = false;    // this thread's rows
+        bool rescale_w = false;  // any row of the warp
         uint64_t rs_a = 0ull, rs_b = 0ull;
         // A later unmasked tile of rows that already have a finite running max
-        // computes P against that max at once and reduces max(x) in the same
-        // loop; only when some row's max rose by more than 2^kRescaleLog2
-        // (rare) is P recomputed against the new max.  Same results as taking
-        // the max first: m only moves when the block raises it past the
-        // threshold, and then to the block max.
-        const bool spec =
-            !masked && j > 0 && __all_sync(0xffffffffu, m_a != -INFINITY && m_b != -INFINITY);
+        // computes P against that max at once, without the tile max; only
+        // when some row's max rose by more than 2^kRescaleLog2 (rare, screened
+        // by the P sums) is the max taken and P recomputed against it.  Same
+        // results as taking the max first: m only moves when the block raises
+        // it past the threshold, and then to the block max.
+        const bool spec = !masked && j > 0 && all_finite;
         if (spec) {
           // P(tt-1)'s stores (and any O rescale) landed while this tile's
           // scores were loaded: publish them now.
@@ -663,38 +647,55 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&p_ready[(tt - 1) % kSBufs]);
           tr(kEvSmPLo, warp >> 2, tt - 1);
-          float xa = -INFINITY, xb = -INFINITY;
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             uint32_t pk[16];
-            p_rows_max<kEmu>(s + 32 * half, c, -m_a, -m_b, rs_a, rs_b, pk, xa, xb);
+            p_rows<kEmu, false>(s + 32 * half, c, -m_a, -m_b, rs_a, rs_b, pk);
             tmem_st_16x128b_x8(tS + 32 * half, pk);
           }
-          xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 1));
-          xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 1));
-          xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 2));
-          xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 2));
           tr(kEvSmMaxDone, warp >> 2, tt);
-          if (xa > kRescaleLog2) {
-            f_a = ex2_approx(-xa);
-            m_a += xa;
-            rescale = true;
-          }
-          if (xb > kRescaleLog2) {
-            f_b = ex2_approx(-xb);
-            m_b += xb;
-            rescale = true;
-          }
-          if (__any_sync(0xffffffffu, rescale)) {
-            // Rare: redo P against the raised maxima.
-            tmem_wait_st();
-            rs_a = 0ull;
-            rs_b = 0ull;
+          // Some x of the tile exceeds kRescaleLog2 only if some P value
+          // exceeds kRescaleP, and then so does the sum of its lane (all terms
+          // are non-negative): the partial sums screen for the rare case, and
+          // only then are the exact maxima taken.
+          float q0, q1, q2, q3;
+          f2_unpack(rs_a, q0, q1);
+          f2_unpack(rs_b, q2, q3);
+          if (__any_sync(0xffffffffu, fmaxf(fmaxf(q0, q1), fmaxf(q2, q3)) > kRescaleP)) {
+            float ma = -INFINITY, mb = -INFINITY;
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              uint32_t pk[16];
-              p_rows<kEmu, false>(s + 32 * half, c, -m_a, -m_b, rs_a, rs_b, pk);
-              tmem_st_16x128b_x8(tS + 32 * half, pk);
+            for (int g = 0; g < 16; ++g) {
+              ma = fmax3(ma, s[4 * g], s[4 * g + 1]);
+              mb = fmax3(mb, s[4 * g + 2], s[4 * g + 3]);
+            }
+            // fma is monotone in s for c >= 0: the max of x is x of the max.
+            float xa = fmaf(ma, c, -m_a), xb = fmaf(mb, c, -m_b);
+            xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 1));
+            xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 1));
+            xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 2));
+            xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 2));
+            if (xa > kRescaleLog2) {
+              f_a = ex2_approx(-xa);
+              m_a += xa;
+              rescale = true;
+            }
+            if (xb > kRescaleLog2) {
+              f_b = ex2_approx(-xb);
+              m_b += xb;
+              rescale = true;
+            }
+            rescale_w = __any_sync(0xffffffffu, rescale);
+            if (rescale_w) {
+              // Redo P against the raised maxima.
+              tmem_wait_st();
+              rs_a = 0ull;
+              rs_b = 0ull;
+#pragma unroll
+              for (int half = 0; half < 2; ++half) {
+                uint32_t pk[16];
+                p_rows<kEmu, false>(s + 32 * half, c, -m_a, -m_b, rs_a, rs_b, pk);
+                tmem_st_16x128b_x8(tS + 32 * half, pk);
+              }
             }
           }
         } else {
@@ -762,6 +763,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             m_b = mx_b;
             rescale = true;
           }
+          rescale_w = __any_sync(0xffffffffu, rescale);
+          all_finite = __all_sync(0xffffffffu, m_a != -INFINITY && m_b != -INFINITY);
           const float nm_a = (m_a == -INFINITY) ? 0.0f : -m_a;
           const float nm_b = (m_b == -INFINITY) ? 0.0f : -m_b;
           const float sc = masked ? 1.0f : c;  // masked scores are pre-scaled
@@ -788,7 +791,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld_16x256b_x16(tmem_base + lane_addr + static_cast<uint32_t>(nb * 128), sr);
           }
         }
-        if (__any_sync(0xffffffffu, rescale) && j > 0) {
+        if (rescale_w && j > 0) {
           // Rare: rescale the O rows whose maximum jumped, once PV(tt-1) has
           // completed; PV(tt) waits for the P barriers below.
           if (!warp_wait(pv_done, static_cast<uint32_t>(tt - 1) & 1u, kSitePvDone)) {
@@ -851,6 +854,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++li;
     }
   } else {
+    setmaxnreg_dec<kEpiRegs>();
     // ================= epilogue (warps 8-11) =================
     const uint32_t quad = warp & 3u;
     const int row = static_cast<int>(quad * 32 + lane);

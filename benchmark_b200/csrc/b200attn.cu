@@ -189,6 +189,18 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   auto kernel = b200::attn::attention_fwd_kernel<D, EMU, TRACE>;
   b200_status st = ensure_smem_attr(kernel, C::kSmemBytes, &attr_done);
   if (st != B200_OK) return st;
+  // The kernel moves registers between warpgroups (setmaxnreg); the split is
+  // sized for exactly kLaunchRegs per thread at launch, and an increase that
+  // the pool cannot satisfy would never complete.  Refuse any other build.
+  static const int launch_regs = [kernel] {
+    cudaFuncAttributes a{};
+    return cudaFuncGetAttributes(&a, kernel) == cudaSuccess ? a.numRegs : -1;
+  }();
+  if (launch_regs != b200::attn::kLaunchRegs)
+    return fail(B200_EUNSUPPORTED,
+                "attention: kernel has %d registers per thread at launch; its register "
+                "split needs exactly %d",
+                launch_regs, b200::attn::kLaunchRegs);
 
   CUtensorMap qm, km, vm, om;
   const uint64_t pq = static_cast<uint64_t>(s.B) * s.Hq;

@@ -105,11 +105,11 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t 
 }
 
 // Record a timeout (first site wins) and return.  Never traps.
-__device__ __noinline__ void report_timeout(uint32_t site) {
+__device__ __forceinline__ void report_timeout(uint32_t site) {
   atomicCAS(&g_status, 0u, kStatusTimeout | ((site & 0xffu) << 8));
 }
 
-__device__ __noinline__ bool mbar_wait_slow(uint32_t addr, uint32_t parity, uint32_t site,
+__device__ __forceinline__ bool mbar_wait_slow(uint32_t addr, uint32_t parity, uint32_t site,
                                             uint64_t limit_ns, uint32_t sleep_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
@@ -155,11 +155,13 @@ __device__ __forceinline__ bool mbar_test3(uint32_t a0, uint32_t p0, uint32_t a1
   return ok != 0;
 }
 
-__device__ __noinline__ bool mbar_wait3_slow(uint32_t a0, uint32_t p0, uint32_t a1, uint32_t p1,
+__device__ __forceinline__ bool mbar_wait3_slow(uint32_t a0, uint32_t p0, uint32_t a1, uint32_t p1,
                                              uint32_t a2, uint32_t p2, uint32_t site) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_test3(a0, p0, a1, p1, a2, p2)) return true;
+    if (mbar_try_wait_sleep(a0, p0, 20000u) && mbar_try_wait_sleep(a1, p1, 20000u) &&
+        mbar_try_wait_sleep(a2, p2, 20000u))
+      return true;
     if ((it & 31u) == 0) {
       if (*reinterpret_cast<volatile uint32_t*>(&g_status) != 0u) return false;
       if (globaltimer_ns() - t0 > kDefaultWaitLimitNs) {
@@ -181,6 +183,22 @@ __device__ __forceinline__ bool mbar_wait3(uint32_t a0, uint32_t p0, uint32_t a1
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Per-warpgroup register re-balancing.  Every warp of a warpgroup executes
+// the same instruction.  An increase waits until the block's pool (threads x
+// registers per thread at launch) has the registers, so the caller must make
+// the warpgroups' new counts sum to exactly that pool.
+// ---------------------------------------------------------------------------
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ---------------------------------------------------------------------------
@@ -639,16 +657,18 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// exp2 of two values on the FMA pipe, for inputs in [-126, 127):
+// exp2 of two values on the FMA pipe (inputs clamped to [-126, 126]):
 //   x = j + r with j = round(x) (adding 1.5 * 2^23 leaves round(x) in the low
 //   mantissa bits of t), r in [-0.5, 0.5];  2^r ~ c0 + r(c1 + r(c2 + r c3)),
 //   a degree-3 minimax fit of the relative error (7.5e-5) produced by
 //   benchmark_b200/csrc/fit_exp2_poly.py;  2^j is applied by adding j << 23
 //   to the exponent field (t's bit pattern << 23 is exactly j << 23).
-// Inputs are clamped to >= -126 so the exponent never underflows.
+// Inputs are clamped to [-126, 126] so the exponent field never under- or
+// overflows (larger inputs give 2^126, still far above any rescale bound).
 __device__ __forceinline__ void exp2_fma_x2(float x0, float x1, float& y0, float& y1) {
   const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
-  const uint64_t x = f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const uint64_t x =
+      f2_pack(fminf(fmaxf(x0, -126.0f), 126.0f), fminf(fmaxf(x1, -126.0f), 126.0f));
   const uint64_t t = f2_add(x, magic);
   const uint64_t r = f2_sub(x, f2_sub(t, magic));
   uint64_t p = f2_fma(f2_pack(0.0551716685295105f, 0.0551716685295105f), r,
