@@ -91,7 +91,6 @@ struct Params {
   int causal;      // bottom-right aligned
   int causal_off;  // Skv - Sq
   float scale_log2;  // softmax_scale * log2(e)
-  int stagger_cycles;  // start delay of softmax warps 4-7 (bounded, clock64 cycles)
   // Clock trace (kTrace instantiations only): per-role record regions of
   // trace_cap records (2 x u64: (event << 32 | tile << 24 | iter), clock64)
   // for CTA trace_cta.  Role r (0 TMA, 1 MMA, 2/3 softmax keys 0-63/64-127,
@@ -103,9 +102,9 @@ struct Params {
 
 // Clock-trace events (kTrace); names in benchmark_b200/trace.py.
 enum : uint32_t {
-  kEvTmaK = 1, kEvTmaV, kEvMmaS, kEvMmaPvLo, kEvMmaPvHi, kEvSmWait, kEvSmReady, kEvSmLdDone,
-  kEvSmMaxDone, kEvSmPLo, kEvSmPHi, kEvEpiBegin, kEvEpiEnd, kEvMmaWait, kEvMmaEnd, kEvMmaGo,
-  kEvTmaQ, kEvSmPComputed, kEvSmStored
+  kEvTmaK = 1, kEvTmaV, kEvMmaS, kEvMmaPvLo, kEvMmaPvHi, kEvSmWait, kEvSmPfTested, kEvSmLdDone,
+  kEvSmMaxDone, kEvSmPLo, kEvSmPfIssued, kEvEpiBegin, kEvEpiEnd, kEvMmaWait, kEvMmaEnd, kEvMmaGo,
+  kEvTmaQ, kEvSmPComputed, kEvSmStored, kEvSmStWaited, kEvSmScreened, kEvSmLDone
 };
 
 template <bool kTrace>
@@ -582,14 +581,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     Tracer<kTrace> tr(p, 2 + static_cast<int>(warp >> 2), trace_cta && quad == 0 && lane == 0);
     int t = 0, li = 0;
     bool ok = true;
-    // Warps w and w+4 share a scheduler and would otherwise run their exp2
-    // phases in lockstep; starting the second one a part-tile later lets one
-    // warp's exp2 overlap the other's loads, max and bookkeeping.
-    if ((warp >> 2) != 0 && p.stagger_cycles > 0) {
-      const long long t_start = clock64();
-      while (clock64() - t_start < p.stagger_cycles) {
-      }
-    }
 #pragma unroll 1
     for (int r = 0; r < rounds && ok; ++r) {
       const int k = item_index(p, r);
@@ -602,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Running max of scaled scores (log2 units) and this thread's share of
       // the row sums, for rows a and b.
       float m_a = -INFINITY, m_b = -INFINITY;
-      float l_a = 0.0f, l_b = 0.0f;
+      uint64_t l2_a = 0ull, l2_b = 0ull;  // packed pairs: even and odd keys
       // S(tt) lives in sr once loaded; the load of a tile's successor is
       // issued as soon as the tile's P is computed, so its latency overlaps
       // the P stores and the bookkeeping.
@@ -630,8 +621,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool masked = kbase + kBN > it.min_lim;  // uniform across the tile
         float f_a = 1.0f, f_b = 1.0f;
         bool rescale = false;    // this thread's rows
-        bool rescale_w = false;  // any row of the warp
         uint64_t rs_a = 0ull, rs_b = 0ull;
+        // Readiness of S(tt+1), tested right after this tile's P loop so that
+        // the test's latency overlaps the work that follows.
+        const int nb = (tt + 1) % kSBufs;
+        bool ready = false;
+        // Rescale the O rows whose maximum jumped, once PV(tt-1) has
+        // completed (PV(tt) waits for this tile's P barrier); rare.
+        auto rescale_o = [&]() {
+          if (!warp_wait(pv_done, static_cast<uint32_t>(tt - 1) & 1u, kSitePvDone)) {
+            ok = false;
+            return;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c0 = 0; c0 < D; c0 += 64) {
+            uint32_t o[32];
+            tmem_ld_16x256b_x8(tO + c0, o);
+            tmem_wait_ld(o);
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              o[4 * g + 0] = __float_as_uint(__uint_as_float(o[4 * g + 0]) * f_a);
+              o[4 * g + 1] = __float_as_uint(__uint_as_float(o[4 * g + 1]) * f_a);
+              o[4 * g + 2] = __float_as_uint(__uint_as_float(o[4 * g + 2]) * f_b);
+              o[4 * g + 3] = __float_as_uint(__uint_as_float(o[4 * g + 3]) * f_b);
+            }
+            tmem_st_16x256b_x8(tO + c0, o);
+          }
+        };
         // A later unmasked tile of rows that already have a finite running max
         // computes P against that max at once, without the tile max; only
         // when some row's max rose by more than 2^kRescaleLog2 (rare, screened
@@ -643,6 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // P(tt-1)'s stores (and any O rescale) landed while this tile's
           // scores were loaded: publish them now.
           tmem_wait_st();
+          tr(kEvSmStWaited, warp >> 2, tt);
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&p_ready[(tt - 1) % kSBufs]);
@@ -653,6 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             p_rows<kEmu, false>(s + 32 * half, c, -m_a, -m_b, rs_a, rs_b, pk);
             tmem_st_16x128b_x8(tS + 32 * half, pk);
           }
+          ready = mbar_try_wait(smem_u32(&s_ready[nb]), static_cast<uint32_t>((tt + 1) / kSBufs) & 1u);
           tr(kEvSmMaxDone, warp >> 2, tt);
           // Some x of the tile exceeds kRescaleLog2 only if some P value
           // exceeds kRescaleP, and then so does the sum of its lane (all terms
@@ -661,7 +680,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           float q0, q1, q2, q3;
           f2_unpack(rs_a, q0, q1);
           f2_unpack(rs_b, q2, q3);
-          if (__any_sync(0xffffffffu, fmaxf(fmaxf(q0, q1), fmaxf(q2, q3)) > kRescaleP)) {
+          const bool big = __any_sync(0xffffffffu, fmaxf(fmaxf(q0, q1), fmaxf(q2, q3)) > kRescaleP);
+          tr(kEvSmScreened, warp >> 2, tt);
+          if (big) {
             float ma = -INFINITY, mb = -INFINITY;
 #pragma unroll
             for (int g = 0; g < 16; ++g) {
@@ -684,8 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               m_b += xb;
               rescale = true;
             }
-            rescale_w = __any_sync(0xffffffffu, rescale);
-            if (rescale_w) {
+            if (__any_sync(0xffffffffu, rescale)) {
               // Redo P against the raised maxima.
               tmem_wait_st();
               rs_a = 0ull;
@@ -696,6 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 p_rows<kEmu, false>(s + 32 * half, c, -m_a, -m_b, rs_a, rs_b, pk);
                 tmem_st_16x128b_x8(tS + 32 * half, pk);
               }
+              rescale_o();
             }
           }
         } else {
@@ -763,7 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             m_b = mx_b;
             rescale = true;
           }
-          rescale_w = __any_sync(0xffffffffu, rescale);
+          const bool rescale_w = __any_sync(0xffffffffu, rescale);
           all_finite = __all_sync(0xffffffffu, m_a != -INFINITY && m_b != -INFINITY);
           const float nm_a = (m_a == -INFINITY) ? 0.0f : -m_a;
           const float nm_b = (m_b == -INFINITY) ? 0.0f : -m_b;
@@ -778,48 +799,22 @@ __global__ void __launch_bounds__(kThreads, 1)
               p_rows<kEmu, false>(s + 32 * half, sc, nm_a, nm_b, rs_a, rs_b, pk);
             tmem_st_16x128b_x8(tS + 32 * half, pk);
           }
+          ready = mbar_try_wait(smem_u32(&s_ready[nb]), static_cast<uint32_t>((tt + 1) / kSBufs) & 1u);
+          if (rescale_w && j > 0) rescale_o();
         }
         tr(kEvSmPComputed, warp >> 2, tt);
         // S(tt+1), if it is this item's and already computed: start its load.
-        if (j + 1 < it.n) {
-          const int nb = (tt + 1) % kSBufs;
-          const bool ready = mbar_try_wait(smem_u32(&s_ready[nb]),
-                                           static_cast<uint32_t>((tt + 1) / kSBufs) & 1u);
-          have_s = __all_sync(0xffffffffu, ready);
-          if (have_s) {
-            tc_fence_after();
-            tmem_ld_16x256b_x16(tmem_base + lane_addr + static_cast<uint32_t>(nb * 128), sr);
-          }
-        }
-        if (rescale_w && j > 0) {
-          // Rare: rescale the O rows whose maximum jumped, once PV(tt-1) has
-          // completed; PV(tt) waits for the P barriers below.
-          if (!warp_wait(pv_done, static_cast<uint32_t>(tt - 1) & 1u, kSitePvDone)) {
-            ok = false;
-          } else {
-            tc_fence_after();
-#pragma unroll 1
-            for (int c0 = 0; c0 < D; c0 += 64) {
-              uint32_t o[32];
-              tmem_ld_16x256b_x8(tO + c0, o);
-              tmem_wait_ld(o);
-#pragma unroll
-              for (int g = 0; g < 8; ++g) {
-                o[4 * g + 0] = __float_as_uint(__uint_as_float(o[4 * g + 0]) * f_a);
-                o[4 * g + 1] = __float_as_uint(__uint_as_float(o[4 * g + 1]) * f_a);
-                o[4 * g + 2] = __float_as_uint(__uint_as_float(o[4 * g + 2]) * f_b);
-                o[4 * g + 3] = __float_as_uint(__uint_as_float(o[4 * g + 3]) * f_b);
-              }
-              tmem_st_16x256b_x8(tO + c0, o);
-            }
-          }
+        have_s = __all_sync(0xffffffffu, ready) && j + 1 < it.n && ok;
+        tr(kEvSmPfTested, warp >> 2, tt);
+        if (have_s) {
+          tc_fence_after();
+          tmem_ld_16x256b_x16(tmem_base + lane_addr + static_cast<uint32_t>(nb * 128), sr);
+          tr(kEvSmPfIssued, warp >> 2, tt);
         }
         tr(kEvSmStored, warp >> 2, tt);
-        float r0, r1;
-        f2_unpack(rs_a, r0, r1);
-        l_a = l_a * f_a + (r0 + r1);
-        f2_unpack(rs_b, r0, r1);
-        l_b = l_b * f_b + (r0 + r1);
+        l2_a = f2_fma(l2_a, f2_pack(f_a, f_a), rs_a);
+        l2_b = f2_fma(l2_b, f2_pack(f_b, f_b), rs_b);
+        tr(kEvSmLDone, warp >> 2, tt);
         if (!ok) break;
       }
       if (ok && it.n > 0) {
@@ -838,6 +833,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       // Row sums over the four threads of each row, handed to the epilogue
       // once it has finished the previous item (li - 1) and read its sums.
+      float l_a, l_b;
+      {
+        float e0, e1;
+        f2_unpack(l2_a, e0, e1);
+        l_a = e0 + e1;
+        f2_unpack(l2_b, e0, e1);
+        l_b = e0 + e1;
+      }
       l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
       l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
       l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);

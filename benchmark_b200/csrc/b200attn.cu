@@ -160,9 +160,6 @@ b200_status check_attention_args(const void* q, const void* k, const void* v, co
 // Measured on B200 (c2: d128, c4: d64 workloads): one pair in eight on the
 // FMA pipe for d128, two for d64, where MUFU is the tighter pipe.
 constexpr int kDefaultEmuD128 = 1;
-// Start delay (cycles) of the second softmax warp of each scheduler;
-// B200_ATTN_STAGGER overrides it (0..100000).
-constexpr int kDefaultStagger = 0;
 constexpr int kDefaultEmuD64 = 2;
 
 int exp2_emu_setting(int D) {
@@ -225,14 +222,6 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   p.causal = s.causal;
   p.causal_off = s.Skv - s.Sq;
   p.scale_log2 = s.scale * 1.4426950408889634f;
-  {
-    static const int stagger = [] {
-      const char* e = std::getenv("B200_ATTN_STAGGER");
-      const int v = e ? std::atoi(e) : kDefaultStagger;
-      return v < 0 ? 0 : (v > 100000 ? 100000 : v);
-    }();
-    p.stagger_cycles = stagger;
-  }
   p.trace = tr.buf;
   p.trace_cap = tr.cap;
   p.trace_cta = tr.cta;

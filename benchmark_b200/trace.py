@@ -23,9 +23,10 @@ import torch
 from . import _lib, ops
 
 EVENTS = {1: "tma_k", 2: "tma_v", 3: "mma_s", 4: "mma_pv_lo", 5: "mma_pv_hi", 6: "sm_wait",
-          7: "sm_ready", 8: "sm_ld_done", 9: "sm_max_done", 10: "sm_p_lo", 11: "sm_p_hi",
-          12: "epi_begin", 13: "epi_end", 14: "mma_wait", 15: "mma_end", 16: "mma_go",
-          17: "tma_q", 18: "sm_p_computed", 19: "sm_p_stored"}
+          7: "sm_pf_tested", 8: "sm_ld_done", 9: "sm_max_done", 10: "sm_p_lo",
+          11: "sm_pf_issued", 12: "epi_begin", 13: "epi_end", 14: "mma_wait", 15: "mma_end",
+          16: "mma_go", 17: "tma_q", 18: "sm_p_computed", 19: "sm_p_stored",
+          20: "sm_st_waited", 21: "sm_screened", 22: "sm_l_done"}
 ROLES = {0: "tma", 1: "mma", 2: "softmax0", 3: "softmax1", 4: "epilogue"}
 
 

@@ -1,5 +1,8 @@
 """CPU checks of the clock-trace decoder (benchmark_b200/trace.py): record
 layout and per-tile stage arithmetic on synthetic records."""
+import re
+from pathlib import Path
+
 import numpy as np
 
 from benchmark_b200 import trace
@@ -33,9 +36,16 @@ def test_summarize_stage_lengths():
     assert st["mma.softmax0_p_to_pv_hi_issue"][0] == 80
 
 
+def _kernel_event_count():
+    """Number of members of the kernel's clock-trace event enum (values 1..n)."""
+    src = (Path(trace.__file__).parent / "csrc" / "attention_kernel.cuh").read_text()
+    body = re.search(r"enum : uint32_t \{\s*(kEvTmaK = 1,[^}]*)\}", src).group(1)
+    return len([m for m in body.replace("\n", " ").split(",") if m.strip()])
+
+
 def test_event_and_role_tables_cover_the_kernel_enums():
-    # Events 1..19 and roles 0..4 as written by the kernel's Tracer.
-    assert sorted(trace.EVENTS) == list(range(1, 20))
+    # One name per event the kernel's Tracer writes (1..n) and roles 0..4.
+    assert sorted(trace.EVENTS) == list(range(1, _kernel_event_count() + 1))
     assert sorted(trace.ROLES) == [0, 1, 2, 3, 4]
     assert len(set(trace.EVENTS.values())) == len(trace.EVENTS)
 
