@@ -663,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tr(kEvSmStWaited, warp >> 2, tt);
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&p_ready[(tt - 1) % kSBufs]);
+          mbar_arrive_warp(&p_ready[(tt - 1) % kSBufs]);
           tr(kEvSmPLo, warp >> 2, tt - 1);
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
@@ -765,7 +765,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_ready[(tt - 1) % kSBufs]);
+            mbar_arrive_warp(&p_ready[(tt - 1) % kSBufs]);
             tr(kEvSmPLo, warp >> 2, tt - 1);
           }
           // Running-max update with lazy rescaling (per row; the four
@@ -822,7 +822,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_ready[(t + it.n - 1) % kSBufs]);
+        mbar_arrive_warp(&p_ready[(t + it.n - 1) % kSBufs]);
         tr(kEvSmPLo, warp >> 2, t + it.n - 1);
       }
       if (have_s) {
@@ -852,7 +852,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         lsum[qb * 128 + rb] = l_b;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&l_ready[qb]);
+      mbar_arrive_warp(&l_ready[qb]);
       t += it.n;
       ++li;
     }

@@ -157,10 +157,12 @@ b200_status check_attention_args(const void* q, const void* k, const void* v, co
 
 // FMA-pipe exp2 share (pairs of every 8) per head_dim; B200_ATTN_EXP2_EMU
 // overrides it for tuning sweeps (values without an instantiation are rejected).
-// Measured on B200 (c2: d128, c4: d64 workloads): one pair in eight on the
-// FMA pipe for d128, two for d64, where MUFU is the tighter pipe.
-constexpr int kDefaultEmuD128 = 1;
-constexpr int kDefaultEmuD64 = 2;
+// Measured on B200 (c2: d128, c4: d64 workloads): none for d128, whose
+// softmax tile is bound by its control latencies rather than MUFU (one pair
+// in eight lost 1.6 %), and one pair in eight for d64, where MUFU is the
+// tighter pipe.
+constexpr int kDefaultEmuD128 = 0;
+constexpr int kDefaultEmuD64 = 1;
 
 int exp2_emu_setting(int D) {
   static const int env_value = [] {
