@@ -625,7 +625,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Readiness of S(tt+1), tested right after this tile's P loop so that
         // the test's latency overlaps the work that follows.
         const int nb = (tt + 1) % kSBufs;
-        bool ready = false;
+        bool ready = false;      // this lane's test
+        bool ready_all = false;  // the warp's vote on it
         // Rescale the O rows whose maximum jumped, once PV(tt-1) has
         // completed (PV(tt) waits for this tile's P barrier); rare.
         auto rescale_o = [&]() {
@@ -681,6 +682,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           f2_unpack(rs_a, q0, q1);
           f2_unpack(rs_b, q2, q3);
           const bool big = __any_sync(0xffffffffu, fmaxf(fmaxf(q0, q1), fmaxf(q2, q3)) > kRescaleP);
+          // Both votes in flight before the first branch on either.
+          ready_all = __all_sync(0xffffffffu, ready);
           tr(kEvSmScreened, warp >> 2, tt);
           if (big) {
             float ma = -INFINITY, mb = -INFINITY;
@@ -800,11 +803,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_16x128b_x8(tS + 32 * half, pk);
           }
           ready = mbar_try_wait(smem_u32(&s_ready[nb]), static_cast<uint32_t>((tt + 1) / kSBufs) & 1u);
+          ready_all = __all_sync(0xffffffffu, ready);
           if (rescale_w && j > 0) rescale_o();
         }
         tr(kEvSmPComputed, warp >> 2, tt);
         // S(tt+1), if it is this item's and already computed: start its load.
-        have_s = __all_sync(0xffffffffu, ready) && j + 1 < it.n && ok;
+        have_s = ready_all && j + 1 < it.n && ok;
         tr(kEvSmPfTested, warp >> 2, tt);
         if (have_s) {
           tc_fence_after();

@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -20,7 +21,6 @@
 #include <cublas_v2.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
-#include <map>
 
 namespace {
 
@@ -62,10 +62,89 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// Encoded tensor maps, cached per (base, shape, box) so repeated calls on the
+// same buffers skip the driver encode (a map holds only the address and the
+// geometry, so a buffer freed and reallocated at the same address with the
+// same shape reuses a valid map).  A fixed direct-mapped table: no host
+// allocation, and a collision only costs a fresh encode.
+struct MapKey {
+  const void* base;
+  uint64_t d0, d1, d2;
+  uint32_t box0, box1, rank;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && d0 == o.d0 && d1 == o.d1 && d2 == o.d2 && box0 == o.box0 &&
+           box1 == o.box1 && rank == o.rank;
+  }
+};
+
+class MapCache {
+ public:
+  bool find(const MapKey& k, CUtensorMap* out) {
+    std::lock_guard<std::mutex> lock(mu_);
+    const Slot& e = slots_[index(k)];
+    if (!e.used || !(e.key == k)) return false;
+    *out = e.map;
+    return true;
+  }
+  void put(const MapKey& k, const CUtensorMap& m) {
+    std::lock_guard<std::mutex> lock(mu_);
+    Slot& e = slots_[index(k)];
+    e.key = k;
+    e.map = m;
+    e.used = true;
+  }
+
+ private:
+  static constexpr size_t kSlots = 256;
+  struct Slot {
+    MapKey key{};
+    CUtensorMap map{};
+    bool used = false;
+  };
+  static size_t index(const MapKey& k) {
+    uint64_t h = reinterpret_cast<uintptr_t>(k.base) * 0x9E3779B97F4A7C15ull;
+    for (uint64_t v : {k.d0, k.d1, k.d2, static_cast<uint64_t>(k.box0) << 32 | k.box1,
+                       static_cast<uint64_t>(k.rank)})
+      h = (h ^ v) * 0x100000001B3ull;
+    return static_cast<size_t>(h >> 32) % kSlots;
+  }
+  std::mutex mu_;
+  Slot slots_[kSlots];
+};
+
+MapCache& map_cache() {
+  static MapCache c;
+  return c;
+}
+
+b200_status encode_bf16_3d_uncached(CUtensorMap* map, const void* base, uint64_t d0,
+                                    uint64_t d1, uint64_t d2, uint32_t box0, uint32_t box1);
+b200_status encode_bf16_2d_uncached(CUtensorMap* map, const void* base, uint64_t d0,
+                                    uint64_t d1, uint32_t box0, uint32_t box1);
+
 // 3-D bf16 tensor [d2][d1][d0] (d0 contiguous), 128-byte swizzled boxes of
 // box0 x box1 x 1 elements.
 b200_status encode_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
                            uint64_t d2, uint32_t box0, uint32_t box1) {
+  const MapKey key{base, d0, d1, d2, box0, box1, 3};
+  if (map_cache().find(key, map)) return B200_OK;
+  const b200_status st = encode_bf16_3d_uncached(map, base, d0, d1, d2, box0, box1);
+  if (st == B200_OK) map_cache().put(key, *map);
+  return st;
+}
+
+// 2-D bf16 tensor [d1][d0] (d0 contiguous), 128-byte swizzled boxes.
+b200_status encode_bf16_2d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                           uint32_t box0, uint32_t box1) {
+  const MapKey key{base, d0, d1, 1, box0, box1, 2};
+  if (map_cache().find(key, map)) return B200_OK;
+  const b200_status st = encode_bf16_2d_uncached(map, base, d0, d1, box0, box1);
+  if (st == B200_OK) map_cache().put(key, *map);
+  return st;
+}
+
+b200_status encode_bf16_3d_uncached(CUtensorMap* map, const void* base, uint64_t d0,
+                                    uint64_t d1, uint64_t d2, uint32_t box0, uint32_t box1) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(B200_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
   const cuuint64_t dims[3] = {d0, d1, d2};
@@ -83,9 +162,8 @@ b200_status encode_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint
   return B200_OK;
 }
 
-// 2-D bf16 tensor [d1][d0] (d0 contiguous), 128-byte swizzled boxes.
-b200_status encode_bf16_2d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
-                           uint32_t box0, uint32_t box1) {
+b200_status encode_bf16_2d_uncached(CUtensorMap* map, const void* base, uint64_t d0,
+                                    uint64_t d1, uint32_t box0, uint32_t box1) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(B200_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
   const cuuint64_t dims[2] = {d0, d1};
