@@ -12,6 +12,9 @@
  *   - bf16 tensors are passed as raw 16-bit words (uint16_t storage).
  *   - Calls are asynchronous on `stream` (NULL = legacy default stream) and
  *     use the calling thread's current CUDA device.
+ *   - TMA tensor maps are encoded on the first call for a (pointer, shape)
+ *     and kept in a fixed-size table, so repeated calls on the same buffers
+ *     skip the driver encode.
  *   - Errors are returned as b200_status, never by exit(); a message for the
  *     most recent failure on the calling thread is in b200_last_error().
  *   - Device-side waits are bounded.  A kernel whose pipeline wait runs out
