@@ -40,10 +40,10 @@
 //
 // Softmax per tile: a thread reads 32 scores of each of its two rows
 // (16x256b TMEM loads); where a row max is needed it is completed by two
-// shuffles, and the running max m is kept in log2 units.  O and the row sums are rescaled only
-// when a block raises m by more than kRescaleLog2 (otherwise P values up to
-// 2^kRescaleLog2 accumulate unscaled: exact in fp32, O / l unchanged), after
-// PV(t-1) has completed.  P is stored with 16x128b stores, whose column
+// shuffles, and the running max m is kept in log2 units.  O and the row sums
+// are rescaled only when a block raises m by more than kRescaleLog2
+// (otherwise P values up to 2^kRescaleLog2 accumulate unscaled: exact in
+// fp32, O / l unchanged), after PV(t-1) has completed.  P is stored with 16x128b stores, whose column
 // order matches the key pairs each thread holds.
 //
 // Every wait is bounded (ptx.cuh).  A timeout sets the device status word;
@@ -581,6 +581,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     Tracer<kTrace> tr(p, 2 + static_cast<int>(warp >> 2), trace_cta && quad == 0 && lane == 0);
     int t = 0, li = 0;
     bool ok = true;
+    // K/V tiles this CTA processes in all (the global tile sequence t).
+    int g_total = 0;
+    for (int r = 0; r < rounds; ++r) {
+      const int k = item_index(p, r);
+      if (k < p.n_items) g_total += decode_item(p, k).n;
+    }
+    // S(tt) lives in sr once loaded; the load of its successor is issued as
+    // soon as tile tt's P is computed, so its latency overlaps the P stores
+    // and the bookkeeping.  For d=64 this also crosses item boundaries
+    // (measured +2 % on config 4; for d=128 it cost 0.5 %).
+    constexpr bool kPrefetchAcrossItems = D == 64;
+    uint32_t sr[64];
+    bool have_s = false;
 #pragma unroll 1
     for (int r = 0; r < rounds && ok; ++r) {
       const int k = item_index(p, r);
@@ -594,11 +607,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the row sums, for rows a and b.
       float m_a = -INFINITY, m_b = -INFINITY;
       uint64_t l2_a = 0ull, l2_b = 0ull;  // packed pairs: even and odd keys
-      // S(tt) lives in sr once loaded; the load of a tile's successor is
-      // issued as soon as the tile's P is computed, so its latency overlaps
-      // the P stores and the bookkeeping.
-      uint32_t sr[64];
-      bool have_s = false;
       bool all_finite = false;  // every row of this warp has a finite running max
 #pragma unroll 1
       for (int j = 0; j < it.n; ++j) {
@@ -808,7 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tr(kEvSmPComputed, warp >> 2, tt);
         // S(tt+1), if it is this item's and already computed: start its load.
-        have_s = ready_all && j + 1 < it.n && ok;
+        have_s = ready_all && (kPrefetchAcrossItems ? tt + 1 < g_total : j + 1 < it.n) && ok;
         tr(kEvSmPfTested, warp >> 2, tt);
         if (have_s) {
           tc_fence_after();
@@ -828,11 +836,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         mbar_arrive_warp(&p_ready[(t + it.n - 1) % kSBufs]);
         tr(kEvSmPLo, warp >> 2, t + it.n - 1);
-      }
-      if (have_s) {
-        // Abandoned prefetch (only after an abort): let the load land.
-        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
       }
       if (!ok) break;
       // Row sums over the four threads of each row, handed to the epilogue
@@ -859,6 +862,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_warp(&l_ready[qb]);
       t += it.n;
       ++li;
+    }
+    if (have_s) {
+      // Abandoned prefetch (only after an abort): let the load land.
+      tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
     }
   } else {
     setmaxnreg_dec<kEpiRegs>();
