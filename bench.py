@@ -591,6 +591,9 @@ def main() -> None:
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     w = WORKLOADS[args.workload]
+    # stdout carries exactly one JSON line: any NCCL log output (its version
+    # banner included, printed under some NCCL_DEBUG settings) goes to stderr.
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     if args.impl == "reference":
         run_reference_arm(args, w)
     elif w.get("kind") == "gemm":
