@@ -592,6 +592,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // and the bookkeeping.  For d=64 this also crosses item boundaries
     // (measured +2 % on config 4; for d=128 it cost 0.5 %).
     constexpr bool kPrefetchAcrossItems = D == 64;
+    // Where a tile's P is published (waiting for its stores, then one arrive
+    // per warp): for d=128 at the end of the tile itself, after the load of
+    // S(tt+1) is issued (+0.7 % on config 2); for d=64 at the start of the
+    // next tile, once its scores have landed (1.6 % better on config 4).
+    constexpr bool kPublishAtTileEnd = D == 128;
     uint32_t sr[64];
     bool have_s = false;
 #pragma unroll 1
@@ -666,14 +671,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         // it past the threshold, and then to the block max.
         const bool spec = !masked && j > 0 && all_finite;
         if (spec) {
-          // P(tt-1)'s stores (and any O rescale) landed while this tile's
-          // scores were loaded: publish them now.
-          tmem_wait_st();
-          tr(kEvSmStWaited, warp >> 2, tt);
-          tc_fence_before();
-          __syncwarp();
-          mbar_arrive_warp(&p_ready[(tt - 1) % kSBufs]);
-          tr(kEvSmPLo, warp >> 2, tt - 1);
+          if constexpr (!kPublishAtTileEnd) {
+            // P(tt-1)'s stores (and any O rescale) landed while this tile's
+            // scores were loaded: publish them now.
+            tmem_wait_st();
+            tr(kEvSmStWaited, warp >> 2, tt);
+            tc_fence_before();
+            __syncwarp();
+            mbar_arrive_warp(&p_ready[(tt - 1) % kSBufs]);
+            tr(kEvSmPLo, warp >> 2, tt - 1);
+          }
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             uint32_t pk[16];
@@ -770,7 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
           mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
           tr(kEvSmMaxDone, warp >> 2, tt);
-          if (j > 0) {
+          if (!kPublishAtTileEnd && j > 0) {
             // P(tt-1)'s stores (and any O rescale) landed while this tile's
             // scores were loaded and reduced: publish them now.
             tmem_wait_st();
@@ -823,13 +830,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_16x256b_x16(tmem_base + lane_addr + static_cast<uint32_t>(nb * 128), sr);
           tr(kEvSmPfIssued, warp >> 2, tt);
         }
+        if (kPublishAtTileEnd && ok) {
+          // Publish P(tt) (and any O rescale) while S(tt+1) is on its way.
+          tmem_wait_st();
+          tr(kEvSmStWaited, warp >> 2, tt);
+          tc_fence_before();
+          __syncwarp();
+          mbar_arrive_warp(&p_ready[sb]);
+          tr(kEvSmPLo, warp >> 2, tt);
+        }
         tr(kEvSmStored, warp >> 2, tt);
         l2_a = f2_fma(l2_a, f2_pack(f_a, f_a), rs_a);
         l2_b = f2_fma(l2_b, f2_pack(f_b, f_b), rs_b);
         tr(kEvSmLDone, warp >> 2, tt);
         if (!ok) break;
       }
-      if (ok && it.n > 0) {
+      if (!kPublishAtTileEnd && ok && it.n > 0) {
         // The item's last P.
         tmem_wait_st();
         tc_fence_before();
