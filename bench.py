@@ -62,6 +62,25 @@ WORKLOADS = {
 NCU_TRAFFIC_BYTES = {"c2": 515.41e6, "gemm": 1152.5e6}
 
 
+# The JSON result line goes to the process's original stdout; everything else
+# written to file descriptor 1 (library banners such as NCCL's version line)
+# is sent to stderr, so stdout carries exactly one line.
+_RESULT_OUT = None
+
+
+def claim_stdout() -> None:
+    global _RESULT_OUT
+    if _RESULT_OUT is None:
+        sys.stdout.flush()
+        _RESULT_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    print(json.dumps(line), file=out, flush=True)
+
+
 def load_peaks() -> tuple[dict, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -241,7 +260,7 @@ def run_reference_arm(args, w: dict) -> None:
                   f"{' causal' if w['causal'] else ''} per step (1 head of K/V each)")
         config = {"workload": w["name"], "B": w["b"], "H": w["h"], "N": w["n"], "D": w["d"],
                   "causal": w["causal"], "sampled": True}
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": GEMM_METRIC if gemm else METRIC, "value": value,
         "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
@@ -252,7 +271,7 @@ def run_reference_arm(args, w: dict) -> None:
                          "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
 
 
 # ---------------------------------------------------------------------------
@@ -454,7 +473,7 @@ def run_gemm_arm(args, w: dict) -> None:
         "cpu_baseline": cpu,
         "lib": _lib.LIB_PATH.name,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_gpu_arm(args, w: dict) -> None:
@@ -566,7 +585,7 @@ def run_gpu_arm(args, w: dict) -> None:
         "cpu_baseline": cpu,
         "lib": _lib.LIB_PATH.name,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main() -> None:
@@ -591,9 +610,11 @@ def main() -> None:
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     w = WORKLOADS[args.workload]
-    # stdout carries exactly one JSON line: any NCCL log output (its version
-    # banner included, printed under some NCCL_DEBUG settings) goes to stderr.
+    # stdout carries exactly one JSON line: NCCL's log output goes to stderr,
+    # and so does anything else a library writes to file descriptor 1 (NCCL
+    # prints its version banner there under some NCCL_DEBUG settings).
     os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+    claim_stdout()
     if args.impl == "reference":
         run_reference_arm(args, w)
     elif w.get("kind") == "gemm":

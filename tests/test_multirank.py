@@ -59,8 +59,22 @@ def test_reference_arm_two_ranks_under_torchrun():
            "--workload", "c1", "--cpu-rows", "2"]
     r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
-    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
-    assert len(lines) == 1, r.stdout
+    lines = r.stdout.splitlines()
+    assert len(lines) == 1 and lines[0].startswith("{"), r.stdout
     line = json.loads(lines[0])
     assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["value"] > 0
     assert line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_library_output_on_fd1_goes_to_stderr():
+    """A banner a library writes straight to file descriptor 1 (as NCCL does
+    with its version line) must not reach stdout, which holds only the JSON
+    result line."""
+    code = ("import os, sys; sys.path.insert(0, '.'); import bench; bench.claim_stdout(); "
+            "os.write(1, b'NCCL version banner\\n'); print('stray print'); "
+            "bench.emit({'value': 1.0})")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True,
+                       timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.splitlines() == ['{"value": 1.0}'], r.stdout
+    assert "NCCL version banner" in r.stderr and "stray print" in r.stderr
