@@ -587,11 +587,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int k = item_index(p, r);
       if (k < p.n_items) g_total += decode_item(p, k).n;
     }
-    // S(tt) lives in sr once loaded; the load of its successor is issued as
-    // soon as tile tt's P is computed, so its latency overlaps the P stores
-    // and the bookkeeping.  For d=64 this also crosses item boundaries
-    // (measured +2 % on config 4; for d=128 it cost 0.5 %).
-    constexpr bool kPrefetchAcrossItems = D == 64;
+    // S(tt) lives in sr once loaded; the load of its successor in the global
+    // tile sequence (also across an item boundary) is issued as soon as tile
+    // tt's P is computed, so its latency overlaps the P stores and the
+    // bookkeeping.
     // Where a tile's P is published (waiting for its stores, then one arrive
     // per warp): for d=128 at the end of the tile itself, after the load of
     // S(tt+1) is issued (+0.7 % on config 2); for d=64 at the start of the
@@ -823,7 +822,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tr(kEvSmPComputed, warp >> 2, tt);
         // S(tt+1), if it is this item's and already computed: start its load.
-        have_s = ready_all && (kPrefetchAcrossItems ? tt + 1 < g_total : j + 1 < it.n) && ok;
+        have_s = ready_all && tt + 1 < g_total && ok;
         tr(kEvSmPfTested, warp >> 2, tt);
         if (have_s) {
           tc_fence_after();

@@ -127,6 +127,24 @@ def test_baseline_config2_full_size():
         gate(o1h[b, h:h + 1, r0:r0 + 128], ref, f"rows b{b} h{h} r{r0}")
 
 
+def test_config4_d64_full_size():
+    """BASELINE config 4 per-GPU shard (B8 H16 N2048 d64, sigma 0.5): ~14 work
+    items per CTA, so every CTA crosses item boundaries many times (the d=64
+    kernel loads the next item's first scores ahead).  Full tensor vs the
+    scalar kernel, oracle rows on a sample of heads."""
+    q, k, v = normal_inputs(8, 16, 16, 2048, 2048, 64, seed=4, sigma=0.5)
+    o = ops.attention_fwd(q, k, v)
+    s = ops.attention_fwd(q, k, v, scalar=True)
+    ops.check()
+    diff = (o.float() - s.float()).abs()
+    assert diff.max().item() <= 2e-2 and diff.mean().item() <= 2e-3, (diff.max(), diff.mean())
+    qh, kh, vh = to_host_bits(q), to_host_bits(k), to_host_bits(v)
+    oh = to_host_f32(o)
+    for b, h, r0 in ((0, 0, 0), (7, 15, 1920), (4, 9, 1000)):
+        ref = oracle.attention_rows(qh, kh, vh, b, h, h + 1, r0, r0 + 128)
+        gate(oh[b, h:h + 1, r0:r0 + 128], ref, f"rows b{b} h{h} r{r0}")
+
+
 def test_config3_causal_long_sample():
     """BASELINE config 3 shape per GPU shard (H=8 of 64, N=16384, causal):
     oracle rows of the last tiles (the longest KV range) and the first."""
