@@ -591,11 +591,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // tile sequence (also across an item boundary) is issued as soon as tile
     // tt's P is computed, so its latency overlaps the P stores and the
     // bookkeeping.
-    // Where a tile's P is published (waiting for its stores, then one arrive
-    // per warp): for d=128 at the end of the tile itself, after the load of
-    // S(tt+1) is issued (+0.7 % on config 2); for d=64 at the start of the
-    // next tile, once its scores have landed (1.6 % better on config 4).
-    constexpr bool kPublishAtTileEnd = D == 128;
     uint32_t sr[64];
     bool have_s = false;
 #pragma unroll 1
@@ -670,16 +665,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // it past the threshold, and then to the block max.
         const bool spec = !masked && j > 0 && all_finite;
         if (spec) {
-          if constexpr (!kPublishAtTileEnd) {
-            // P(tt-1)'s stores (and any O rescale) landed while this tile's
-            // scores were loaded: publish them now.
-            tmem_wait_st();
-            tr(kEvSmStWaited, warp >> 2, tt);
-            tc_fence_before();
-            __syncwarp();
-            mbar_arrive_warp(&p_ready[(tt - 1) % kSBufs]);
-            tr(kEvSmPLo, warp >> 2, tt - 1);
-          }
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             uint32_t pk[16];
@@ -776,15 +761,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
           mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
           tr(kEvSmMaxDone, warp >> 2, tt);
-          if (!kPublishAtTileEnd && j > 0) {
-            // P(tt-1)'s stores (and any O rescale) landed while this tile's
-            // scores were loaded and reduced: publish them now.
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            mbar_arrive_warp(&p_ready[(tt - 1) % kSBufs]);
-            tr(kEvSmPLo, warp >> 2, tt - 1);
-          }
           // Running-max update with lazy rescaling (per row; the four
           // threads of a row hold the same values, so they decide alike).
           if (m_a == -INFINITY) {
@@ -821,16 +797,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (rescale_w && j > 0) rescale_o();
         }
         tr(kEvSmPComputed, warp >> 2, tt);
-        // S(tt+1), if it is this item's and already computed: start its load.
+        // S(tt+1) (the next item's first tile after an item's last), if it is
+        // already computed: its load starts once P(tt) is published.
         have_s = ready_all && tt + 1 < g_total && ok;
         tr(kEvSmPfTested, warp >> 2, tt);
-        if (have_s) {
-          tc_fence_after();
-          tmem_ld_16x256b_x16(tmem_base + lane_addr + static_cast<uint32_t>(nb * 128), sr);
-          tr(kEvSmPfIssued, warp >> 2, tt);
-        }
-        if (kPublishAtTileEnd && ok) {
-          // Publish P(tt) (and any O rescale) while S(tt+1) is on its way.
+        if (ok) {
+          // Publish P(tt) (and any O rescale) before S(tt+1)'s load is
+          // issued: the store wait and fence would otherwise also wait for
+          // that load (measured 2 % slower).
           tmem_wait_st();
           tr(kEvSmStWaited, warp >> 2, tt);
           tc_fence_before();
@@ -838,19 +812,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_warp(&p_ready[sb]);
           tr(kEvSmPLo, warp >> 2, tt);
         }
+        if (have_s) {
+          tc_fence_after();
+          tmem_ld_16x256b_x16(tmem_base + lane_addr + static_cast<uint32_t>(nb * 128), sr);
+          tr(kEvSmPfIssued, warp >> 2, tt);
+        }
         tr(kEvSmStored, warp >> 2, tt);
         l2_a = f2_fma(l2_a, f2_pack(f_a, f_a), rs_a);
         l2_b = f2_fma(l2_b, f2_pack(f_b, f_b), rs_b);
         tr(kEvSmLDone, warp >> 2, tt);
         if (!ok) break;
-      }
-      if (!kPublishAtTileEnd && ok && it.n > 0) {
-        // The item's last P.
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        mbar_arrive_warp(&p_ready[(t + it.n - 1) % kSBufs]);
-        tr(kEvSmPLo, warp >> 2, t + it.n - 1);
       }
       if (!ok) break;
       // Row sums over the four threads of each row, handed to the epilogue
