@@ -59,7 +59,7 @@ WORKLOADS = {
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel,
 # from the ncu captures in profiles/attention_fwd_d128_c2_b4h32n4096.md and
 # profiles/gemm_bf16_pair_8192_b_row_major.md (None: not captured).
-NCU_TRAFFIC_BYTES = {"c2": 515.41e6, "gemm": 1152.5e6}
+NCU_TRAFFIC_BYTES = {"c2": 515.99e6, "gemm": 1152.5e6}
 
 
 # The JSON result line goes to the process's original stdout; everything else
