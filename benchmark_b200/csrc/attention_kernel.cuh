@@ -16,6 +16,9 @@
 //   warp  13    tcgen05.mma issuer (whole warp, one elected lane issues)
 //   warp  14    TMA producer for the V ring (its own thread, so K loads run
 //               ahead of the V ring's slower turnover)
+//   warp  15    idle; it completes warpgroup 3, so that each warpgroup can
+//               move its register budget with setmaxnreg (softmax 184,
+//               epilogue 56, producers/issuer 88 registers per thread)
 //
 // TMEM (512 columns): three S buffers [0,128) [128,256) [256,384) rotate over
 // the global tile sequence; O at [384, 384+D).  P (bf16 pairs) overwrites the
@@ -43,8 +46,13 @@
 // shuffles, and the running max m is kept in log2 units.  O and the row sums
 // are rescaled only when a block raises m by more than kRescaleLog2
 // (otherwise P values up to 2^kRescaleLog2 accumulate unscaled: exact in
-// fp32, O / l unchanged), after PV(t-1) has completed.  P is stored with 16x128b stores, whose column
-// order matches the key pairs each thread holds.
+// fp32, O / l unchanged), after PV(t-1) has completed.  Unmasked tiles after
+// an item's first compute P against the running max directly and take the
+// tile max only when the P sums show a jump (rare).  P is stored with
+// 16x128b stores, whose column order matches the key pairs each thread
+// holds, and published (store wait, fence, one arrive per warp) at the end
+// of its own tile, before the next tile's scores are loaded: a TMEM store
+// wait or fence behind an outstanding TMEM load waits for that load too.
 //
 // Every wait is bounded (ptx.cuh).  A timeout sets the device status word;
 // the epilogue warps, which meet at a named barrier, agree on aborting
