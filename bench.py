@@ -13,6 +13,13 @@ One JSON line on rank 0 (see the project's benchmark contract):
   roofline   dominant kernel vs the measured bf16 tensor peak
   cpu_baseline  the reference's CPU attention (oracle/_ref) on a bounded
              sample, on this host's cores (rank 0, N=1 only)
+  strong     (every N) BASELINE configs 3 and 4 as fixed total problems split
+             across the N ranks: config 3 (B1 H64 N16384 d128 causal) by head,
+             config 4 (B64 H16 N2048 d64) by batch; box TFLOP/s and the
+             slowest rank's time
+  configs    (N=1) every other BASELINE config on this GPU: config 1, configs
+             3 and 4 in full, and the GEMM at 8192^3 and 16384^3 with cuBLAS
+             timed before and after it on the same operands
 
 --impl reference runs the reference's CPU implementation of the path (the
 compiled reference code in oracle/_ref, else the oracle restatement) on all
@@ -39,27 +46,33 @@ METRIC = "attention fwd TFLOPS per GPU and per box at 1/2/4/8 B200; % of bf16 te
 GEMM_METRIC = "bf16 GEMM TFLOP/s (tcgen05 vs cuBLAS) at 8192^3"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# Per-GPU workloads.  "b" is the per-GPU batch.
+# BASELINE.json configs.  "b" and "h" are the per-GPU batch and heads of a
+# weak-scaling workload; a "split" workload is a fixed total problem whose
+# heads ("h") or batches ("b") are divided among the ranks.
 WORKLOADS = {
     "c2": dict(name="attn_b4_h32_n4096_d128", b=4, h=32, n=4096, d=128, causal=False,
                sigma=1.0),
     "c1": dict(name="attn_b1_h8_n1024_d128", b=1, h=8, n=1024, d=128, causal=False, sigma=1.0),
-    # config 3: H=64 sharded by head over N GPUs; per GPU shard of 8 heads at N=8.
-    "c3": dict(name="attn_b1_h64_n16384_d128_causal_per_gpu_h8", b=1, h=8, n=16384, d=128,
-               causal=True, sigma=1.0),
-    # config 4: B=64 sharded by batch over 8 GPUs: 8 per GPU.
-    "c4": dict(name="attn_b64_h16_n2048_d64_per_gpu_b8", b=8, h=16, n=2048, d=64, causal=False,
-               sigma=0.5),
-    # The GEMM path (5.GEMM): 8192^3, A and B ~ U(-1,1), B stored [K, N] as
-    # the reference stores it; each rank multiplies its own pair (weak scaling).
+    # config 3: B=1, H=64, N=16384 causal, split by head over the ranks
+    "c3": dict(name="attn_b1_h64_n16384_d128_causal", b=1, h=64, n=16384, d=128, causal=True,
+               sigma=1.0, split="h"),
+    # config 4: B=64, H=16, N=2048, d=64, sigma 0.5, split by batch over the ranks
+    "c4": dict(name="attn_b64_h16_n2048_d64", b=64, h=16, n=2048, d=64, causal=False,
+               sigma=0.5, split="b"),
+    # The GEMM path (5.GEMM): A and B ~ U(-1,1), B stored [K, N] as the
+    # reference stores it; each rank multiplies its own pair (weak scaling).
     "gemm": dict(name="gemm_bf16_m8192_n8192_k8192_b_row_major", kind="gemm", m=8192, n=8192,
                  k=8192),
+    "gemm16k": dict(name="gemm_bf16_m16384_n16384_k16384_b_row_major", kind="gemm", m=16384,
+                    n=16384, k=16384),
 }
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel,
-# from the ncu captures in profiles/attention_fwd_d128_c2_b4h32n4096.md and
-# profiles/gemm_bf16_pair_8192_b_row_major.md (None: not captured).
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel
+# of each workload, from the ncu captures summarised in profiles/ (None: not
+# captured).
 NCU_TRAFFIC_BYTES = {"c2": 515.99e6, "gemm": 1152.5e6}
+
+L2_BYTES = 126 * 2**20
 
 
 # The JSON result line goes to the process's original stdout; everything else
@@ -91,6 +104,36 @@ def load_peaks() -> tuple[dict, str]:
 def attention_flops(w: dict) -> float:
     f = 4.0 * w["b"] * w["h"] * w["n"] * w["n"] * w["d"]
     return f / 2 if w["causal"] else f
+
+
+def shard(w: dict, rank: int, world: int) -> tuple[dict, int]:
+    """This rank's part of workload w and the global index of its first
+    element.  Weak workloads: every rank gets (b, h) of its own batch slice of
+    a [b * world, h, n, d] tensor.  Split workloads: the fixed [b, h, n, d]
+    problem's heads (B = 1) or batches are divided evenly among the ranks."""
+    split = w.get("split")
+    if split is None:
+        part = dict(w)
+    elif split == "h":
+        if w["b"] != 1 or w["h"] % world:
+            raise ValueError(f"{w['name']}: {w['h']} heads do not split over {world} ranks")
+        part = dict(w, h=w["h"] // world)
+    else:
+        if w["b"] % world:
+            raise ValueError(f"{w['name']}: batch {w['b']} does not split over {world} ranks")
+        part = dict(w, b=w["b"] // world)
+    per = part["b"] * part["h"] * part["n"] * part["d"]
+    return part, rank_index_base(rank, per)
+
+
+def l2_note(read_bytes: int, flushed: bool) -> str:
+    mib = read_bytes / 2**20
+    if read_bytes > L2_BYTES:
+        return f"inputs larger than L2 ({mib:.0f} MiB read per step, L2 126 MiB)"
+    if flushed:
+        return (f"inputs fit in L2 ({mib:.1f} MiB); L2 flushed by a 256 MiB write between "
+                "timed steps, each step timed alone")
+    return f"inputs fit in L2 ({mib:.1f} MiB); not flushed: L2-warm figure"
 
 
 # ---------------------------------------------------------------------------
@@ -357,234 +400,328 @@ def pipelined_e2e(args, inputs, out, compute, stream, world, dev, barrier, flops
             "ms_per_step": ms, "pipelined": "2 buffer sets, H2D / compute / D2H streams"}
 
 
-def run_e2e(args, w, q, k, v, o, stream, world, dev, barrier, flops) -> dict:
+class Ranks:
+    """torch.distributed plumbing of one GPU arm process (world 1: no-ops)."""
+
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            import datetime
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=self.dev)
+
+    def barrier(self) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier(device_ids=[self.local])
+
+    def max(self, value: float) -> float:
+        return max_over_ranks(value, self.world, self.dev)
+
+    def close(self) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier(device_ids=[self.local])
+            dist.destroy_process_group()
+
+
+def attention_inputs(part: dict, index_base: int, seed: int, dev):
+    """Q, K, V (seeded, by global element index) and O for one rank's part."""
+    import torch
+
+    from benchmark_b200 import ops
+    q = torch.empty((part["b"], part["h"], part["n"], part["d"]), dtype=torch.bfloat16,
+                    device=dev)
+    k = torch.empty_like(q)
+    v = torch.empty_like(q)
+    o = torch.empty_like(q)
+    for t, tid in ((q, 0), (k, 1), (v, 2)):
+        ops.fill_normal_(t, seed, tid, 0.0, part["sigma"], index_base=index_base)
+    torch.cuda.synchronize()
+    return q, k, v, o
+
+
+def time_steps(step, steps: int, warmup: int, ranks: Ranks, stream, flush=None,
+               clocks: ClockSampler | None = None) -> tuple[float, float]:
+    """(this rank's ms per step, slowest rank's ms per step) of `step`.
+
+    Without `flush` the steps run back to back between two events.  With it,
+    `flush()` runs before every step outside the timed events (an L2 flush for
+    inputs that fit in L2) and each step is timed alone."""
+    import contextlib
+
+    import torch
+
+    from benchmark_b200 import ops
+    for _ in range(warmup):
+        step()
+    ops.check(stream)
+    ranks.barrier()
+    torch.cuda.synchronize()
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    with clocks if clocks is not None else contextlib.nullcontext():
+        if flush is None:
+            start, stop = ev(), ev()
+            start.record(stream)
+            for _ in range(steps):
+                step()
+            stop.record(stream)
+            torch.cuda.synchronize()
+            ms = start.elapsed_time(stop) / steps
+        else:
+            pairs = []
+            for _ in range(steps):
+                flush()
+                e0, e1 = ev(), ev()
+                e0.record(stream)
+                step()
+                e1.record(stream)
+                pairs.append((e0, e1))
+            torch.cuda.synchronize()
+            ms = sum(e0.elapsed_time(e1) for e0, e1 in pairs) / steps
+    ranks.barrier()
+    ops.check(stream)
+    return ms, ranks.max(ms)
+
+
+def l2_flusher(dev):
+    import torch
+    buf = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
+    return lambda: buf.fill_(1)
+
+
+def attention_roofline(part: dict, ms_local: float, key: str, peaks: dict, peak_src: str,
+                       q_bytes: int) -> dict:
+    flops = attention_flops(part)
+    achieved = flops / (ms_local * 1e-3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES.get(key),
+            "algorithmic_bytes": 4 * q_bytes,  # Q, K, V read + O written once
+            "kernel": f"attention_fwd_kernel<{part['d']}>",
+            "peak_source": f"{peak_src} bf16_tflops (burst)"}
+
+
+def measure_attention(key: str, args, ranks: Ranks, stream, peaks, peak_src, steps: int,
+                      warmup: int, with_clocks: bool = False) -> dict:
+    """One attention workload on every rank (its shard); whole-box numbers."""
+    import torch
+
+    from benchmark_b200 import ops
+    w = WORKLOADS[key]
+    part, base = shard(w, ranks.rank, ranks.world)
+    q, k, v, o = attention_inputs(part, base, args.seed, ranks.dev)
+    read_bytes = 3 * q.numel() * q.element_size()
+    flush = l2_flusher(ranks.dev) if read_bytes <= L2_BYTES else None
+
+    def step():
+        ops.attention_fwd(q, k, v, out=o, causal=part["causal"], stream=stream)
+
+    clocks = ClockSampler(ranks.local) if with_clocks else None
+    ms, ms_max = time_steps(step, steps, warmup, ranks, stream, flush, clocks)
+    box_flops = attention_flops(part) * ranks.world
+    r = {"workload": w["name"], "value": box_flops / (ms_max * 1e-3) / 1e12, "unit": "TFLOP/s",
+         "ms_per_step": ms_max, "rank_ms_per_step": ms, "steps": steps, "warmup": warmup,
+         "gpu_launches": steps, "per_rank": {"B": part["b"], "H": part["h"]},
+         "l2": l2_note(read_bytes, flush is not None),
+         "hbm_gbs_algorithmic": ranks.world * 4 * q.numel() * 2 / (ms_max * 1e-3) / 1e9,
+         "exp_per_s": ranks.world * part["b"] * part["h"] * part["n"] * part["n"]
+         / (2 if part["causal"] else 1) / (ms_max * 1e-3),
+         "roofline": attention_roofline(part, ms, key, peaks, peak_src, q.numel() * 2)}
+    if clocks is not None:
+        r["clocks"] = clocks.summary()
+    r["_tensors"] = (q, k, v, o)
+    del q, k, v, o
+    torch.cuda.synchronize()
+    return r
+
+
+def measure_gemm(key: str, args, ranks: Ranks, stream, peaks, peak_src, steps: int,
+                 warmup: int, with_clocks: bool = False) -> dict:
+    """This library's tcgen05 CTA-pair GEMM on C = A @ B with B stored [K, N],
+    every rank on its own operands; cuBLAS on the same operands is timed
+    before and after it and the two are averaged, so a power-capped GPU's
+    drift between the runs favours neither side."""
+    import torch
+
+    from benchmark_b200 import ops
+    w = WORKLOADS[key]
+    M, N, K = w["m"], w["n"], w["k"]
+    a = torch.empty((M, K), dtype=torch.bfloat16, device=ranks.dev)
+    b = torch.empty((K, N), dtype=torch.bfloat16, device=ranks.dev)
+    c = torch.empty((M, N), dtype=torch.bfloat16, device=ranks.dev)
+    ops.fill_uniform_(a, args.seed, 10, -1.0, 1.0,
+                      index_base=rank_index_base(ranks.rank, a.numel()))
+    ops.fill_uniform_(b, args.seed, 11, -1.0, 1.0,
+                      index_base=rank_index_base(ranks.rank, b.numel()))
+    torch.cuda.synchronize()
+    flops = 2.0 * M * N * K
+
+    def timed(impl: str, clocks=None) -> tuple[float, float]:
+        def step():
+            ops.gemm_bf16(a, b, out=c, b_col_major=False, impl=impl, stream=stream)
+        return time_steps(step, steps, warmup, ranks, stream, None, clocks)
+
+    _, ms_cublas_before = timed("cublas")
+    clocks = ClockSampler(ranks.local) if with_clocks else None
+    ms_local, ms_max = timed("tcgen05", clocks)
+    _, ms_cublas_after = timed("cublas")
+    ms_cublas = 0.5 * (ms_cublas_before + ms_cublas_after)
+    box = lambda ms: ranks.world * flops / (ms * 1e-3) / 1e12  # noqa: E731
+    achieved = flops / (ms_local * 1e-3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    algo = 2 * (M * K + K * N + M * N)
+    r = {"workload": w["name"], "value": box(ms_max), "unit": "TFLOP/s", "ms_per_step": ms_max,
+         "rank_ms_per_step": ms_local, "steps": steps, "warmup": warmup,
+         "gpu_launches": steps, "M": M, "N": N, "K": K, "b_layout": "[K,N]",
+         "l2": l2_note(2 * (M * K + K * N), False),
+         "cublas_tflops": box(ms_cublas),
+         "cublas_tflops_before_after": [box(ms_cublas_before), box(ms_cublas_after)],
+         "vs_cublas": ms_cublas / ms_max,
+         "hbm_gbs_algorithmic": ranks.world * algo / (ms_max * 1e-3) / 1e9,
+         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                      "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES.get(key),
+                      "algorithmic_bytes": algo, "kernel": "gemm_bf16_pair_kernel",
+                      "peak_source": f"{peak_src} bf16_tflops (burst)"}}
+    if clocks is not None:
+        r["clocks"] = clocks.summary()
+    r["_tensors"] = (a, b, c)
+    return r
+
+
+def public(entry: dict) -> dict:
+    return {k: v for k, v in entry.items() if not k.startswith("_")}
+
+
+def run_e2e(args, part, q, k, v, o, stream, ranks: Ranks, flops) -> dict:
     from benchmark_b200 import ops
 
     def compute(d_in, d_out):
-        ops.attention_fwd(d_in[0], d_in[1], d_in[2], out=d_out, causal=w["causal"],
+        ops.attention_fwd(d_in[0], d_in[1], d_in[2], out=d_out, causal=part["causal"],
                           stream=stream)
 
-    return pipelined_e2e(args, [q, k, v], o, compute, stream, world, dev, barrier, flops)
+    return pipelined_e2e(args, [q, k, v], o, compute, stream, ranks.world, ranks.dev,
+                         ranks.barrier, flops)
 
 
-def run_gemm_arm(args, w: dict) -> None:
-    """The GEMM path: this library's tcgen05 CTA-pair kernel on C = A @ B with
-    B stored [K, N], every rank on its own operands; cuBLAS on the same
-    operands is reported beside it."""
-    import torch
-    import torch.distributed as dist
-
-    from benchmark_b200 import _lib, ops
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local])
-
-    M, N, K = w["m"], w["n"], w["k"]
-    a = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
-    b = torch.empty((K, N), dtype=torch.bfloat16, device=dev)
-    c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-    ops.fill_uniform_(a, args.seed, 10, -1.0, 1.0, index_base=rank_index_base(rank, a.numel()))
-    ops.fill_uniform_(b, args.seed, 11, -1.0, 1.0, index_base=rank_index_base(rank, b.numel()))
-    torch.cuda.synchronize()
-    stream = torch.cuda.current_stream()
-    flops = 2.0 * M * N * K
-
-    def timed(impl: str) -> float:
-        for _ in range(args.warmup):
-            ops.gemm_bf16(a, b, out=c, b_col_major=False, impl=impl, stream=stream)
-        ops.check(stream)
-        barrier()
-        torch.cuda.synchronize()
-        start = torch.cuda.Event(enable_timing=True)
-        stop = torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(args.steps):
-            ops.gemm_bf16(a, b, out=c, b_col_major=False, impl=impl, stream=stream)
-        stop.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        ops.check(stream)
-        return start.elapsed_time(stop) / args.steps
-
-    # cuBLAS is timed both before and after this kernel on the same operands
-    # and the two are averaged, so a power-capped GPU's drift between the runs
-    # favours neither side.
-    ms_cublas_before = max_over_ranks(timed("cublas"), world, dev)
-    with ClockSampler(local) as clocks:
-        ms_local = timed("tcgen05")
-    ms_max = max_over_ranks(ms_local, world, dev)
-    ms_cublas_after = max_over_ranks(timed("cublas"), world, dev)
-    ms_cublas = 0.5 * (ms_cublas_before + ms_cublas_after)
-    value = world * flops / (ms_max * 1e-3) / 1e12
-
-    def compute(d_in, d_out):
-        ops.gemm_bf16(d_in[0], d_in[1], out=d_out, b_col_major=False, stream=stream)
-
-    e2e = None if args.no_e2e else pipelined_e2e(args, [a, b], c, compute, stream, world, dev,
-                                                 barrier, flops)
-    peaks, peak_src = load_peaks()
-    peak = float(peaks["bf16_tflops"])
-    achieved = flops / (ms_local * 1e-3) / 1e12
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = host_threads()
-        r = gemm_cpu_sample(w, args.cpu_gemm_rows, threads)
-        cpu = {"value": r["flops"] / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": threads,
-               "kind": r["kind"],
-               "sample": (f"{threads} threads x {args.cpu_gemm_rows} rows of C x N={N} x K={K} "
-                          f"({r['seconds']:.1f} s wall)")}
-    if world > 1:
-        dist.barrier(device_ids=[local])
-        dist.destroy_process_group()
-    if rank != 0:
-        return
-    line = {
-        "metric": GEMM_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": f"synthetic: bf16 A, B ~ U(-1,1), counter-based seed {args.seed}",
-        "config": {"workload": w["name"], "M": M, "N": N, "K": K, "b_layout": "[K,N]",
-                   "parallelism": f"dp{world} (independent GEMM per rank)",
-                   "l2": "inputs larger than L2 (256 MiB of A and B per step)"},
-        "cublas_tflops": world * flops / (ms_cublas * 1e-3) / 1e12,
-        "cublas_tflops_before_after": [world * flops / (ms_cublas_before * 1e-3) / 1e12,
-                                       world * flops / (ms_cublas_after * 1e-3) / 1e12],
-        "hbm_gbs_algorithmic": world * 2 * (M * K + K * N + M * N) / (ms_max * 1e-3) / 1e9,
-        "vs_cublas": ms_cublas / ms_max,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES.get(args.workload),
-                     "algorithmic_bytes": 2 * (M * K + K * N + M * N),
-                     "kernel": "gemm_bf16_pair_kernel",
-                     "peak_source": f"{peak_src} bf16_tflops (burst)"},
-        "e2e": e2e,
-        "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
-        "cpu_baseline": cpu,
-        "lib": _lib.LIB_PATH.name,
-    }
-    emit(line)
+def strong_and_configs(args, ranks: Ranks, stream, peaks, peak_src, main_key: str) -> tuple:
+    """The `strong` object (every N) and the `configs` object (N=1 only)."""
+    steps = max(3, min(args.steps, args.config_steps))
+    strong, configs = {}, {}
+    for key in ("c3", "c4"):
+        if args.no_configs:
+            break
+        r = measure_attention(key, args, ranks, stream, peaks, peak_src, steps, 3)
+        strong[key] = {"workload": r["workload"], "value": r["value"], "unit": r["unit"],
+                       "ms_per_step": r["ms_per_step"], "per_rank": r["per_rank"],
+                       "split": "heads" if WORKLOADS[key]["split"] == "h" else "batch",
+                       "n_gpus": ranks.world}
+        if ranks.world == 1 and key != main_key:
+            configs[key] = public(r)
+        del r
+    if ranks.world == 1 and not args.no_configs:
+        for key in ("c1", "gemm", "gemm16k"):
+            if key == main_key:
+                continue
+            fn = measure_gemm if WORKLOADS[key].get("kind") == "gemm" else measure_attention
+            csteps = steps if key != "c1" else max(steps, 50)
+            configs[key] = public(fn(key, args, ranks, stream, peaks, peak_src, csteps, 3))
+    return strong, configs
 
 
 def run_gpu_arm(args, w: dict) -> None:
     import torch
-    import torch.distributed as dist
 
-    from benchmark_b200 import _lib, ops
+    from benchmark_b200 import _lib
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local])
-
-    B, H, N, D = w["b"], w["h"], w["n"], w["d"]
-    q = torch.empty((B, H, N, D), dtype=torch.bfloat16, device=dev)
-    k = torch.empty_like(q)
-    v = torch.empty_like(q)
-    o = torch.empty_like(q)
-    per = q.numel()
-    # this rank's batch slice of the global [B * world, H, N, D] tensors
-    for t, tid in ((q, 0), (k, 1), (v, 2)):
-        ops.fill_normal_(t, args.seed, tid, 0.0, w["sigma"],
-                         index_base=rank_index_base(rank, per))
-    torch.cuda.synchronize()
-
+    ranks = Ranks()
     stream = torch.cuda.current_stream()
-
-    def step():
-        ops.attention_fwd(q, k, v, out=o, causal=w["causal"], stream=stream)
-
-    for _ in range(args.warmup):
-        step()
-    ops.check(stream)
-    barrier()
-    torch.cuda.synchronize()
-
-    start = torch.cuda.Event(enable_timing=True)
-    stop = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        start.record(stream)
-        for _ in range(args.steps):
-            step()
-        stop.record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    ops.check(stream)
-    ms = start.elapsed_time(stop) / args.steps
-    ms_max = max_over_ranks(ms, world, dev)
-    flops = attention_flops(w)
-    value = world * flops / (ms_max * 1e-3) / 1e12
-
-    e2e = None if args.no_e2e else run_e2e(args, w, q, k, v, o, stream, world, dev, barrier,
-                                           flops)
-
     peaks, peak_src = load_peaks()
-    peak = float(peaks["bf16_tflops"])
-    achieved = flops / (ms * 1e-3) / 1e12
-    traffic = NCU_TRAFFIC_BYTES.get(args.workload)
-    algo_bytes = 4 * q.numel() * q.element_size()  # Q, K, V read + O written once
+    gemm = w.get("kind") == "gemm"
+    key = args.workload
+    fn = measure_gemm if gemm else measure_attention
+    main = fn(key, args, ranks, stream, peaks, peak_src, args.steps, args.warmup,
+              with_clocks=True)
+    if gemm:
+        a, b, c = main.pop("_tensors")
+
+        def compute(d_in, d_out):
+            from benchmark_b200 import ops
+            ops.gemm_bf16(d_in[0], d_in[1], out=d_out, b_col_major=False, stream=stream)
+
+        flops = 2.0 * w["m"] * w["n"] * w["k"]
+        e2e = None if args.no_e2e else pipelined_e2e(args, [a, b], c, compute, stream,
+                                                     ranks.world, ranks.dev, ranks.barrier,
+                                                     flops)
+        del a, b, c
+    else:
+        q, k, v, o = main.pop("_tensors")
+        part, _ = shard(w, ranks.rank, ranks.world)
+        e2e = None if args.no_e2e else run_e2e(args, part, q, k, v, o, stream, ranks,
+                                               attention_flops(part))
+        del q, k, v, o
+    torch.cuda.empty_cache()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline:
         threads = host_threads()
-        rows = args.cpu_baseline_rows
-        r = cpu_reference_sample(w, rows, threads)
+        if gemm:
+            rows = args.cpu_gemm_rows
+            r = gemm_cpu_sample(w, rows, threads)
+            sample = f"{threads} threads x {rows} rows of C x N={w['n']} x K={w['k']}"
+        else:
+            rows = args.cpu_baseline_rows
+            r = cpu_reference_sample(w, rows, threads)
+            sample = f"{threads} threads x {rows} query rows x {w['n']} keys x d{w['d']}"
         cpu = {"value": r["flops"] / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": threads,
-               "kind": r["kind"],
-               "sample": (f"{threads} threads x {rows} query rows x {N} keys x d{D} "
-                          f"({r['seconds']:.1f} s wall)")}
+               "kind": r["kind"], "sample": f"{sample} ({r['seconds']:.1f} s wall)"}
 
-    if world > 1:
-        dist.barrier(device_ids=[local])
-        dist.destroy_process_group()
-    if rank != 0:
+    strong, configs = strong_and_configs(args, ranks, stream, peaks, peak_src, key)
+    ranks.close()
+    if ranks.rank != 0:
         return
+    world = ranks.world
+    if gemm:
+        config = {"workload": w["name"], "M": w["m"], "N": w["n"], "K": w["k"],
+                  "b_layout": "[K,N]", "parallelism": f"dp{world} (independent GEMM per rank)",
+                  "l2": main["l2"]}
+        data = f"synthetic: bf16 A, B ~ U(-1,1), counter-based seed {args.seed}"
+        scaling = "weak"
+    else:
+        part, _ = shard(w, 0, world)
+        split = w.get("split")
+        config = {"workload": w["name"], "B_per_gpu": part["b"], "H_per_gpu": part["h"],
+                  "global_B": part["b"] * world if split is None else w["b"],
+                  "H": w["h"], "N": w["n"], "D": w["d"], "causal": w["causal"],
+                  "parallelism": (f"dp{world} (batch-sharded heads, no collective)"
+                                  if split is None else
+                                  f"{'head' if split == 'h' else 'batch'}-split over {world} "
+                                  "ranks, no collective"),
+                  "l2": main["l2"]}
+        data = (f"synthetic: bf16 Q/K/V ~ N(0,{w['sigma']}^2), counter-based seed {args.seed}")
+        scaling = "weak" if split is None else "strong"
     line = {
-        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": f"synthetic: bf16 Q/K/V ~ N(0,{w['sigma']}^2), counter-based seed {args.seed}",
-        "config": {"workload": w["name"], "B_per_gpu": B, "global_B": B * world, "H": H,
-                   "N": N, "D": D, "causal": w["causal"],
-                   "parallelism": f"dp{world} (batch-sharded heads, no collective)",
-                   "l2": (f"inputs larger than L2 ({3 * q.numel() * 2 / 2**20:.0f} MiB of "
-                          "Q/K/V read per step)")},
-        "per_gpu_tflops": value / world,
-        # algorithmic HBM rate (Q+K+V read, O written once) and exp2 rate,
-        # whole box: the config-4 view of the same run
-        "hbm_gbs_algorithmic": world * algo_bytes / (ms_max * 1e-3) / 1e9,
-        "exp_per_s": world * (w["b"] * w["h"] * w["n"] * w["n"] / (2 if w["causal"] else 1))
-        / (ms_max * 1e-3),
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": traffic,
-                     "algorithmic_bytes": algo_bytes,
-                     "kernel": f"attention_fwd_kernel<{D}>",
-                     "peak_source": f"{peak_src} bf16_tflops (burst)"},
-        "e2e": e2e,
-        "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
-        "cpu_baseline": cpu,
-        "lib": _lib.LIB_PATH.name,
+        "metric": GEMM_METRIC if gemm else METRIC, "value": main["value"], "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": main["ms_per_step"], "higher_is_better": True, "scaling": scaling,
+        "vs_baseline": None, "dtype": "bf16", "data": data, "config": config,
+        "per_gpu_tflops": main["value"] / world,
+        "hbm_gbs_algorithmic": main["hbm_gbs_algorithmic"],
     }
+    for k in ("exp_per_s", "cublas_tflops", "cublas_tflops_before_after", "vs_cublas"):
+        if k in main:
+            line[k] = main[k]
+    line.update({
+        "roofline": main["roofline"], "e2e": e2e, "gpu_launches": main["gpu_launches"],
+        "clocks": main.get("clocks"), "cpu_baseline": cpu, "strong": strong or None,
+        "configs": configs or None, "lib": _lib.LIB_PATH.name,
+    })
     emit(line)
 
 
@@ -606,6 +743,10 @@ def main() -> None:
                     help="rows of C per host thread in the CPU GEMM sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the strong-scaling and per-config objects")
+    ap.add_argument("--config-steps", type=int, default=10,
+                    help="timed steps of each strong/configs entry")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -617,8 +758,6 @@ def main() -> None:
     claim_stdout()
     if args.impl == "reference":
         run_reference_arm(args, w)
-    elif w.get("kind") == "gemm":
-        run_gemm_arm(args, w)
     else:
         run_gpu_arm(args, w)
 

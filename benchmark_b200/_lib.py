@@ -41,6 +41,7 @@ _PROTOTYPES = {
     "b200_fill_uniform_bf16": [_vp, _u64, _u64, _u32, _u64, _f, _f, _vp],
     "b200_check": [_vp],
     "b200_selftest_wait_timeout": [_u64, _vp],
+    "b200_selftest_exp2": [_vp, _vp, _vp, _u64, _vp],
     "gemm_bf16": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "gemm_bf16_cublas": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "gemm_f32_reference": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],

@@ -233,23 +233,12 @@ b200_status check_attention_args(const void* q, const void* k, const void* v, co
   return B200_OK;
 }
 
-// FMA-pipe exp2 share (pairs of every 8) per head_dim; B200_ATTN_EXP2_EMU
-// overrides it for tuning sweeps (values without an instantiation are rejected).
-// Measured on B200 (c2: d128, c4: d64 workloads): none for d128, whose
-// softmax tile is bound by its control latencies rather than MUFU (one pair
-// in eight lost 1.6 %), and one pair in eight for d64, where MUFU is the
-// tighter pipe.
+// FMA-pipe exp2 share (pairs of every 8) per head_dim.  Measured on B200
+// (c2: d128, c4: d64 workloads): none for d128, whose softmax tile is bound
+// by its control latencies rather than MUFU (one pair in eight lost 1.6 %),
+// and one pair in eight for d64, where MUFU is the tighter pipe.
 constexpr int kDefaultEmuD128 = 0;
 constexpr int kDefaultEmuD64 = 1;
-
-int exp2_emu_setting(int D) {
-  static const int env_value = [] {
-    const char* e = std::getenv("B200_ATTN_EXP2_EMU");
-    return e ? std::atoi(e) : -1;
-  }();
-  if (env_value >= 0) return env_value;
-  return D == 128 ? kDefaultEmuD128 : kDefaultEmuD64;
-}
 
 struct TraceArgs {
   unsigned long long* buf = nullptr;
@@ -313,20 +302,6 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   return B200_OK;
 }
 
-template <int D>
-b200_status dispatch_attention(const void* q, const void* k, const void* v, void* o,
-                               const AttnShape& s, cudaStream_t stream) {
-  switch (exp2_emu_setting(D)) {
-    case 0: return launch_attention<D, 0>(q, k, v, o, s, stream);
-    case 1: return launch_attention<D, 1>(q, k, v, o, s, stream);
-    case 2: return launch_attention<D, 2>(q, k, v, o, s, stream);
-    case 3: return launch_attention<D, 3>(q, k, v, o, s, stream);
-    case 4: return launch_attention<D, 4>(q, k, v, o, s, stream);
-    default:
-      return fail(B200_EINVAL, "B200_ATTN_EXP2_EMU must be 0..4; got %d", exp2_emu_setting(D));
-  }
-}
-
 b200_status check_gemm_args(const void* A, const void* Bm, const void* C, int M, int N, int K,
                             const char* who) {
   if (!A || !Bm || !C) return fail(B200_EINVAL, "%s: null matrix pointer", who);
@@ -376,8 +351,8 @@ b200_status attention_fwd(const void* q, const void* k, const void* v, void* o, 
                                         softmax_scale, &s);
   if (st != B200_OK) return st;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  return D == 128 ? dispatch_attention<128>(q, k, v, o, s, cs)
-                  : dispatch_attention<64>(q, k, v, o, s, cs);
+  return D == 128 ? launch_attention<128, kDefaultEmuD128>(q, k, v, o, s, cs)
+                  : launch_attention<64, kDefaultEmuD64>(q, k, v, o, s, cs);
 }
 
 b200_status attention_fwd_trace(const void* q, const void* k, const void* v, void* o, int B,
@@ -486,6 +461,38 @@ __global__ void selftest_wait_kernel(uint64_t limit_ns) {
 }
 }  // namespace
 
+namespace {
+// Evaluates the softmax's two exp2 paths elementwise: the FMA-pipe polynomial
+// (exp2_fma_x2, in pairs) and MUFU ex2.approx.ftz.
+__global__ void selftest_exp2_kernel(const float* x, float* y_fma, float* y_mufu, uint64_t n) {
+  const uint64_t i = 2 * (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x);
+  if (i >= n) return;
+  const float x0 = x[i];
+  const float x1 = i + 1 < n ? x[i + 1] : 0.0f;
+  float y0, y1;
+  b200::exp2_fma_x2(x0, x1, y0, y1);
+  y_fma[i] = y0;
+  y_mufu[i] = b200::ex2_approx(x0);
+  if (i + 1 < n) {
+    y_fma[i + 1] = y1;
+    y_mufu[i + 1] = b200::ex2_approx(x1);
+  }
+}
+}  // namespace
+
+extern "C" b200_status b200_selftest_exp2(const float* x, float* y_fma, float* y_mufu,
+                                          uint64_t n, b200_stream_t stream) {
+  if (n == 0) return B200_OK;
+  if (!x || !y_fma || !y_mufu) return fail(B200_EINVAL, "b200_selftest_exp2: null pointer");
+  const uint64_t blocks = (n + 511) / 512;
+  if (blocks > 0x7fffffffull) return fail(B200_EUNSUPPORTED, "b200_selftest_exp2: n too large");
+  selftest_exp2_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                         reinterpret_cast<cudaStream_t>(stream)>>>(x, y_fma, y_mufu, n);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "b200_selftest_exp2 launch");
+  return B200_OK;
+}
+
 extern "C" b200_status b200_selftest_wait_timeout(uint64_t limit_ns, b200_stream_t stream) {
   if (limit_ns < 1000) limit_ns = 1000;
   if (limit_ns > 100000000ull) limit_ns = 100000000ull;
@@ -496,17 +503,6 @@ extern "C" b200_status b200_selftest_wait_timeout(uint64_t limit_ns, b200_stream
 }
 
 namespace {
-
-// Which tcgen05 GEMM kernel gemm_bf16 runs: the CTA-pair 256x256 kernel
-// (default) or the single-CTA 128x256 kernel.  B200_GEMM_KERNEL=single|pair
-// selects one for comparisons.
-bool gemm_use_pair() {
-  static const bool pair = [] {
-    const char* e = std::getenv("B200_GEMM_KERNEL");
-    return !(e && std::strcmp(e, "single") == 0);
-  }();
-  return pair;
-}
 
 b200::gemm::Params gemm_params(int M, int N, int K, int b_col_major, void* C, int bm, int bn,
                                int bk) {
@@ -522,43 +518,10 @@ b200::gemm::Params gemm_params(int M, int N, int K, int b_col_major, void* C, in
   return p;
 }
 
-b200_status launch_gemm_single(const void* A, const void* Bm, void* C, int M, int N, int K,
-                               int b_col_major, cudaStream_t stream) {
-  namespace g = b200::gemm;
-  static unsigned attr_done = 0;
-  b200_status st = ensure_smem_attr(g::gemm_bf16_kernel, g::kSmemBytes, &attr_done);
-  if (st != B200_OK) return st;
-  CUtensorMap am, bm;
-  if ((st = encode_bf16_2d(&am, A, K, M, g::kBK, g::kBM)) != B200_OK) return st;
-  if (b_col_major)
-    st = encode_bf16_2d(&bm, Bm, K, N, g::kBK, g::kBN);
-  else
-    st = encode_bf16_2d(&bm, Bm, N, K, 64, g::kBK);
-  if (st != B200_OK) return st;
-  const g::Params p = gemm_params(M, N, K, b_col_major, C, g::kBM, g::kBN, g::kBK);
-  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
-  if (tiles > 0x7fffffffll) return fail(B200_EUNSUPPORTED, "gemm_bf16: too many tiles");
-  const int grid = static_cast<int>(std::min<long long>(tiles, sm_count()));
-  g::gemm_bf16_kernel<<<grid, g::kThreads, g::kSmemBytes, stream>>>(am, bm, p);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16 launch");
-  return B200_OK;
-}
-
-// Raster group (256-row blocks per group) and the L2 hints of the pair
-// kernel's A and B loads (0 evict_last, 1 evict_first, 2 evict_normal);
-// B200_GEMM_GROUP_M / B200_GEMM_A_POLICY / B200_GEMM_B_POLICY override them
-// for sweeps.  Measured on B200 (B [K,N]): groups of 8 are best at 8192^3
-// (16 costs 0.4 %), groups of 16 at 16384^3 (+2 % over 8); an evict-first
-// hint on B loses 1-8 %.
+// Raster group (256-row blocks per group), measured on B200 (B [K,N]): groups
+// of 8 are best at 8192^3 (16 costs 0.4 %), groups of 16 at 16384^3 (+2 %
+// over 8).
 int gemm_default_group(int K) { return K >= 12288 ? 16 : 8; }
-constexpr int kGemmAPolicy = 0;
-constexpr int kGemmBPolicy = 0;
-
-int gemm_env_int(const char* name, int fallback) {
-  const char* e = std::getenv(name);
-  return e ? std::atoi(e) : fallback;
-}
 
 // Clusters of two that can be resident at once on the current device.
 int pair_clusters_resident() {
@@ -599,9 +562,7 @@ b200_status launch_gemm_pair(const void* A, const void* Bm, void* C, int M, int 
     st = encode_bf16_2d(&bm, Bm, N, K, 64, g::pair::kBK);
   if (st != B200_OK) return st;
   g::Params p = gemm_params(M, N, K, b_col_major, C, g::pair::kBM, g::pair::kBN, g::pair::kBK);
-  p.group_m = gemm_env_int("B200_GEMM_GROUP_M", gemm_default_group(K));
-  p.a_policy = gemm_env_int("B200_GEMM_A_POLICY", kGemmAPolicy);
-  p.b_policy = gemm_env_int("B200_GEMM_B_POLICY", kGemmBPolicy);
+  p.group_m = gemm_default_group(K);
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
   if (tiles > 0x3fffffffll) return fail(B200_EUNSUPPORTED, "gemm_bf16: too many tiles");
   const long long clusters = std::min<long long>(tiles, pair_clusters_resident());
@@ -619,8 +580,7 @@ extern "C" b200_status gemm_bf16(const void* A, const void* Bm, void* C, int M, 
   const b200_status st = check_gemm_args(A, Bm, C, M, N, K, "gemm_bf16");
   if (st != B200_OK) return st;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return gemm_use_pair() ? launch_gemm_pair(A, Bm, C, M, N, K, b_col_major, s)
-                         : launch_gemm_single(A, Bm, C, M, N, K, b_col_major, s);
+  return launch_gemm_pair(A, Bm, C, M, N, K, b_col_major, s);
 }
 
 extern "C" b200_status gemm_bf16_cublas(const void* A, const void* Bm, void* C, int M, int N,

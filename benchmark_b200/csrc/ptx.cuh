@@ -670,18 +670,20 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// exp2 of two values on the FMA pipe (inputs clamped to [-126, 126]):
+// exp2 of two values on the FMA pipe (inputs clamped to [-125, 126]):
 //   x = j + r with j = round(x) (adding 1.5 * 2^23 leaves round(x) in the low
 //   mantissa bits of t), r in [-0.5, 0.5];  2^r ~ c0 + r(c1 + r(c2 + r c3)),
 //   a degree-3 minimax fit of the relative error (7.5e-5) produced by
 //   benchmark_b200/csrc/fit_exp2_poly.py;  2^j is applied by adding j << 23
 //   to the exponent field (t's bit pattern << 23 is exactly j << 23).
-// Inputs are clamped to [-126, 126] so the exponent field never under- or
-// overflows (larger inputs give 2^126, still far above any rescale bound).
+// The clamp keeps the exponent field normal: with j >= -125 and p >= 2^-0.5
+// the sum never reaches the subnormal range (at j = -126 a p just below 1
+// would), and j <= 126 never overflows.  So x < -125 gives 2^-125 (MUFU's
+// ftz form gives 0 below 2^-126) and x > 126 gives 2^126.
 __device__ __forceinline__ void exp2_fma_x2(float x0, float x1, float& y0, float& y1) {
   const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
   const uint64_t x =
-      f2_pack(fminf(fmaxf(x0, -126.0f), 126.0f), fminf(fmaxf(x1, -126.0f), 126.0f));
+      f2_pack(fminf(fmaxf(x0, -125.0f), 126.0f), fminf(fmaxf(x1, -125.0f), 126.0f));
   const uint64_t t = f2_add(x, magic);
   const uint64_t r = f2_sub(x, f2_sub(t, magic));
   uint64_t p = f2_fma(f2_pack(0.0551716685295105f, 0.0551716685295105f), r,

@@ -11,7 +11,9 @@
 //   --validate / --validate-suite           fused kernel vs the scalar kernel
 //   --scalar-validate / --scalar-validate-suite   scalar kernel vs the fused
 //   general shape flags --b --hq --hkv --sq --skv --d --causal --scale
-//   --pattern constant|onehot|rank1|random|normal|uniform  --seed --sigma
+//   --pattern constant|onehot|rank1|random|normal|uniform|reference_bench
+//             --seed --sigma   (benchmark mode: "constant" means seeded normal
+//             data; reference_bench is the reference benchmark's own fill)
 //   --checksum-repeats N (outputs must be bit-identical across repeats)
 // Exit codes as the reference: 0 ok, 1 failure, 2 bad arguments, 77 no SM100.
 //
@@ -107,7 +109,7 @@ bool parse(int argc, char** argv, Args* a) {
   }
   const std::string& p = a->pattern;
   if (p != "constant" && p != "onehot" && p != "rank1" && p != "random" && p != "normal" &&
-      p != "uniform") {
+      p != "uniform" && p != "reference_bench") {
     std::fprintf(stderr, "unknown pattern %s\n", p.c_str());
     return false;
   }
@@ -171,6 +173,18 @@ struct Dev {
 
 bool fill(void* dst, char m, int B, int H, int S, int D, const Args& a, uint32_t tid) {
   const size_t n = static_cast<size_t>(B) * H * S * D;
+  if (a.pattern == "reference_bench") {
+    // The reference benchmark's own data (fill_packed_bf16,
+    // 0.attention/attention.cu:142-147, seeds 3 / 11 / 17 for Q / K / V at
+    // 0.attention/main.cu:2068-2075): bf16 pairs near 1.0, word i =
+    // 0x3f803f80 ^ ((i + seed * 977) & 0x000f000f), so that a same-box
+    // comparison with the reference kernel runs on identical inputs.
+    const uint32_t seed = m == 'q' ? 3u : (m == 'k' ? 11u : 17u);
+    std::vector<uint32_t> w(n / 2);
+    for (size_t i = 0; i < w.size(); ++i)
+      w[i] = 0x3f803f80u ^ ((static_cast<uint32_t>(i) + seed * 977u) & 0x000f000fu);
+    return cudaMemcpy(dst, w.data(), n * 2, cudaMemcpyHostToDevice) == cudaSuccess;
+  }
   if (a.pattern == "normal")
     return b200_fill_normal_bf16(dst, n, a.seed, tid, 0, 0.0f, a.sigma, nullptr) == B200_OK;
   if (a.pattern == "uniform")
@@ -346,26 +360,36 @@ int run_benchmark(const Args& a) {
     if (b200_check(nullptr) != B200_OK) status = "warmup_runtime_failed";
   }
   if (std::strcmp(status, "ok") == 0) {
-    cudaEvent_t e0, e1, t0, t1;
+    // Mean over back-to-back launches between two events (as the reference's
+    // run_kernel times, 0.attention/main.cu:571-597); then a second pass with
+    // an event pair around each launch, still back to back, for min and max.
+    cudaEvent_t e0, e1;
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
-    cudaEventCreate(&t0);
-    cudaEventCreate(&t1);
     cudaEventRecord(e0);
-    for (int i = 0; i < a.iters; ++i) {
-      cudaEventRecord(t0);
+    for (int i = 0; i < a.iters; ++i)
       if (launch() != B200_OK) status = "timed_launch_failed";
-      cudaEventRecord(t1);
-      cudaEventSynchronize(t1);
-      float one = 0;
-      cudaEventElapsedTime(&one, t0, t1);
-      mn = std::min(mn, one);
-      mx = std::max(mx, one);
-    }
     cudaEventRecord(e1);
     cudaEventSynchronize(e1);
     cudaEventElapsedTime(&ms, e0, e1);
     ms /= static_cast<float>(a.iters);
+    std::vector<cudaEvent_t> ev(2 * a.iters);
+    for (auto& e : ev) cudaEventCreate(&e);
+    for (int i = 0; i < a.iters; ++i) {
+      cudaEventRecord(ev[2 * i]);
+      if (launch() != B200_OK) status = "timed_launch_failed";
+      cudaEventRecord(ev[2 * i + 1]);
+    }
+    cudaEventSynchronize(ev.back());
+    for (int i = 0; i < a.iters; ++i) {
+      float one = 0;
+      cudaEventElapsedTime(&one, ev[2 * i], ev[2 * i + 1]);
+      mn = std::min(mn, one);
+      mx = std::max(mx, one);
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
     if (b200_check(nullptr) != B200_OK) status = "timed_runtime_failed";
     cerr = cudaGetLastError();
   }
@@ -385,8 +409,9 @@ int run_benchmark(const Args& a) {
                 "%.6f,%.3f,%.3f,%.3f,%.3f,%.3f,%.6f,%.6f,%.0f,%.3f,%.3f,%.4f,%.3f,%s,%s,%s\n",
                 B, H, N, D, a.causal, a.blocks, a.k_tiles, a.warmup, a.iters, ms, gb, gb, gb, gb,
                 4 * gb, tbps(gb), tbps(gb), tbps(gb), tbps(gb), tbps(4 * gb), mn, mx, flops,
-                tflops / 2, tflops / 2, tflops / 1613.4, tflops, status,
-                cudaGetErrorString(cerr), "seeded_normal_inputs");
+                tflops / 2, tflops / 2, tflops / 1658.2, tflops, status,
+                cudaGetErrorString(cerr),
+                a.pattern == "reference_bench" ? "reference_benchmark_fill" : "seeded_normal_inputs");
   if (!a.csv.empty()) {
     FILE* f = std::fopen(a.csv.c_str(), "w");
     if (f) {

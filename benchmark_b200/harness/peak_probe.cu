@@ -4,7 +4,7 @@
 // 2.TMEM_LDST (TMEM load/store rate) and the exp/MUFU rate its softmax
 // design assumes, plus a plain HBM copy:
 //
-//   peak_probe [--probe mma|tmem|mufu|hbm|all] [--iters N] [--device N]
+//   peak_probe [--probe mma|issue|tmem|mufu|hbm|all] [--iters N] [--device N]
 //
 // One CTA per SM.  Each probe prints one line `probe=... value=... unit=...`
 // with the per-SM cycle count behind it.  Operand values do not matter for a
@@ -135,6 +135,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
   }
 }
 
+// tcgen05.mma M=128 N=128 K=16, both operands in shared memory, issued by
+// `issuers` warps of each CTA (several CTAs per SM when the grid asks for
+// them), each warp into its own 128-column accumulator.  reuse = 1 repeats
+// the same A and B descriptors for every MMA, the pattern of the reference's
+// issue-rate probe (1.mma/mma_throughput_bench.cu:404-460); reuse = 0 walks
+// four K slices of distinct operands, as a kernel's K loop does.  Operands
+// are bf16 near 1.0 (the reference probe's fill).
+__global__ void __launch_bounds__(128) mma_issue_probe(int issuers, int reuse, int iters,
+                                                       unsigned long long* cycles) {
+  __shared__ __align__(1024) uint8_t smem[32768];  // A 128x64 | B 128x64 (K-major SW128)
+  __shared__ uint64_t bar;
+  __shared__ uint32_t slot;
+  for (int i = threadIdx.x; i < 32768 / 4; i += blockDim.x)
+    reinterpret_cast<uint32_t*>(smem)[i] = 0x3f803f80u ^ (static_cast<uint32_t>(i) & 0x000f000fu);
+  fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, static_cast<uint32_t>(issuers));
+    fence_mbar_init();
+  }
+  const uint32_t cols = issuers == 1 ? 128u : (issuers == 2 ? 256u : 512u);
+  if (warp_id() == 0) {
+    tmem_alloc(&slot, cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = slot;
+  unsigned long long t0 = clock64();
+  if (static_cast<int>(warp_id()) < issuers) {
+    const uint32_t idesc = idesc_bf16_f32(128, 128, false, false);
+    const uint64_t da = sdesc_sw128(smem_u32(smem), 16, 1024);
+    const uint64_t db = sdesc_sw128(smem_u32(smem + 16384), 16, 1024);
+    const uint32_t d = tmem + warp_id() * 128u;
+    const uint32_t step = reuse ? 0u : 2u;
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mma_ss_warp(d, da + k * step, db + k * step, idesc, 1u);
+    }
+    mma_commit_warp(&bar);
+  }
+  const bool ok = mbar_wait(&bar, 0, 0x53);
+  const unsigned long long t1 = clock64();
+  if (threadIdx.x == 0) cycles[blockIdx.x] = ok ? t1 - t0 : 0ull;
+  tc_fence_before();
+  __syncthreads();
+  if (warp_id() == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, cols);
+  }
+}
+
 // tcgen05.ld / tcgen05.st 32x32b.x32 by four warps (each its lane quadrant).
 __global__ void __launch_bounds__(128, 1) tmem_probe(int store, int iters,
                                                      unsigned long long* cycles,
@@ -242,7 +294,7 @@ int main(int argc, char** argv) {
       return argv[++i];
     };
     if (f == "--help") {
-      std::printf("peak_probe [--probe mma|tmem|mufu|hbm|all] [--iters N] [--device N]\n");
+      std::printf("peak_probe [--probe mma|issue|tmem|mufu|hbm|all] [--iters N] [--device N]\n");
       return 0;
     } else if (f == "--probe") probe = next();
     else if (f == "--iters") iters = std::atoi(next());
@@ -253,7 +305,8 @@ int main(int argc, char** argv) {
     }
   }
   if (iters < 16 || iters > (1 << 20) ||
-      (probe != "mma" && probe != "tmem" && probe != "mufu" && probe != "hbm" && probe != "all")) {
+      (probe != "mma" && probe != "issue" && probe != "tmem" && probe != "mufu" &&
+       probe != "hbm" && probe != "all")) {
     std::fprintf(stderr, "invalid arguments (see --help)\n");
     return 2;
   }
@@ -317,6 +370,31 @@ int main(int argc, char** argv) {
       const double flops = 2.0 * 256 * n * 16 * 4.0 * iters * pairs;
       std::printf("probe=mma_pair_m256_n%d_ss cycles_per_mma=%.2f value=%.1f unit=TFLOP/s "
                   "ms=%.4f\n", n, per_mma, flops / (ms * 1e-3) / 1e12, ms);
+    }
+  }
+  if (probe == "issue" || probe == "all") {
+    // M128 N128 SS: issue warps per CTA x CTAs per SM (at most four 128-column
+    // accumulators per SM), same or distinct operands.
+    const int combos[6][2] = {{1, 1}, {2, 1}, {4, 1}, {1, 2}, {1, 4}, {2, 2}};
+    for (int reuse = 1; reuse >= 0; --reuse) {
+      for (const auto& c : combos) {
+        const int issuers = c[0], per_sm = c[1];
+        const int grid = sms * per_sm;
+        if (grid > 1024) continue;
+        const double ms = timed([&] {
+          mma_issue_probe<<<grid, 128>>>(issuers, reuse, iters, cyc);
+        });
+        unsigned long long h[1024];
+        cudaMemcpy(h, cyc, grid * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+        unsigned long long mx = 0;
+        for (int i = 0; i < grid; ++i) mx = h[i] > mx ? h[i] : mx;
+        const double mmas_per_sm = 4.0 * iters * issuers * per_sm;
+        const double flops = 2.0 * 128 * 128 * 16 * mmas_per_sm * sms;
+        std::printf("probe=mma_m128_n128_ss_%s issuers_per_cta=%d ctas_per_sm=%d "
+                    "cycles_per_mma_per_sm=%.2f value=%.1f unit=TFLOP/s ms=%.4f\n",
+                    reuse ? "same_operands" : "distinct_operands", issuers, per_sm,
+                    static_cast<double>(mx) / mmas_per_sm, flops / (ms * 1e-3) / 1e12, ms);
+      }
     }
   }
   if (probe == "tmem" || probe == "all") {

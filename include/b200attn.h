@@ -171,6 +171,18 @@ int b200_version(void);
  */
 b200_status b200_selftest_wait_timeout(uint64_t limit_ns, b200_stream_t stream);
 
+/*
+ * Self-test of the softmax's two exp2 implementations: for each of the n fp32
+ * inputs x[i] (device buffers), y_fma[i] = the FMA-pipe polynomial exp2 and
+ * y_mufu[i] = ex2.approx.ftz (MUFU).  The polynomial clamps x to [-126, 126],
+ * so it returns 2^-126 below that range and 2^126 above it; inside it its
+ * relative error is below 7.5e-5 (degree-3 minimax fit).  Stands in for the
+ * reference's software exp2 emulation (0.attention/ptx_wrappers.cuh:711-741),
+ * which has no test of its own.
+ */
+b200_status b200_selftest_exp2(const float* x, float* y_fma, float* y_mufu, uint64_t n,
+                               b200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

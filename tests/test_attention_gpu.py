@@ -127,29 +127,11 @@ def test_baseline_config2_full_size():
         gate(o1h[b, h:h + 1, r0:r0 + 128], ref, f"rows b{b} h{h} r{r0}")
 
 
-def test_config4_d64_full_size():
-    """BASELINE config 4 per-GPU shard (B8 H16 N2048 d64, sigma 0.5): ~14 work
-    items per CTA, so every CTA crosses item boundaries many times (the d=64
-    kernel loads the next item's first scores ahead).  Full tensor vs the
-    scalar kernel, oracle rows on a sample of heads."""
-    q, k, v = normal_inputs(8, 16, 16, 2048, 2048, 64, seed=4, sigma=0.5)
-    o = ops.attention_fwd(q, k, v)
-    s = ops.attention_fwd(q, k, v, scalar=True)
-    ops.check()
-    diff = (o.float() - s.float()).abs()
-    assert diff.max().item() <= 2e-2 and diff.mean().item() <= 2e-3, (diff.max(), diff.mean())
-    qh, kh, vh = to_host_bits(q), to_host_bits(k), to_host_bits(v)
-    oh = to_host_f32(o)
-    for b, h, r0 in ((0, 0, 0), (7, 15, 1920), (4, 9, 1000)):
-        ref = oracle.attention_rows(qh, kh, vh, b, h, h + 1, r0, r0 + 128)
-        gate(oh[b, h:h + 1, r0:r0 + 128], ref, f"rows b{b} h{h} r{r0}")
-
-
-def test_config3_causal_long_sample():
-    """BASELINE config 3 shape per GPU shard (H=8 of 64, N=16384, causal):
-    the full tensor against the scalar kernel, and oracle rows of the last
-    tiles (the longest KV range) and the first."""
-    q, k, v = normal_inputs(1, 8, 8, 16384, 16384, 128, seed=3)
+def test_config3_full_64_heads_causal():
+    """BASELINE config 3 as stated (B1 H64 N16384 d128 causal) on one GPU:
+    8,192 causal work items.  The full tensor against the scalar kernel, and
+    oracle rows of the first, a middle and the last Q tile of four heads."""
+    q, k, v = normal_inputs(1, 64, 64, 16384, 16384, 128, seed=3)
     o = ops.attention_fwd(q, k, v, causal=True)
     s = ops.attention_fwd(q, k, v, causal=True, scalar=True)
     ops.check()
@@ -158,9 +140,47 @@ def test_config3_causal_long_sample():
     del s, diff
     qh, kh, vh = to_host_bits(q), to_host_bits(k), to_host_bits(v)
     oh = to_host_f32(o)
-    for h, r0 in ((0, 16384 - 64), (7, 0), (3, 8192 - 32)):
-        ref = oracle.attention_rows(qh, kh, vh, 0, h, h + 1, r0, r0 + 64, causal=True)
-        gate(oh[0, h:h + 1, r0:r0 + 64], ref, f"causal rows h{h} r{r0}")
+    for h in (0, 21, 42, 63):
+        for r0 in (0, 8192 - 32, 16384 - 64):
+            ref = oracle.attention_rows(qh, kh, vh, 0, h, h + 1, r0, r0 + 32, causal=True)
+            gate(oh[0, h:h + 1, r0:r0 + 32], ref, f"causal rows h{h} r{r0}")
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_config3_head_shards_match_full(world):
+    """Config 3 split by head as bench.py splits it over `world` ranks: each
+    shard, generated from its global element indices, gives the same output
+    bytes as the same heads of the full 64-head problem."""
+    q, k, v = normal_inputs(1, 64, 64, 16384, 16384, 128, seed=3)
+    o = ops.attention_fwd(q, k, v, causal=True)
+    hp = 64 // world
+    per = hp * 16384 * 128
+    for r in (0, world - 1):
+        qs = torch.empty((1, hp, 16384, 128), dtype=torch.bfloat16, device="cuda")
+        ks, vs = torch.empty_like(qs), torch.empty_like(qs)
+        for t, tid in ((qs, 0), (ks, 1), (vs, 2)):
+            ops.fill_normal_(t, 3, tid, 0.0, 1.0, index_base=r * per)
+        os_ = ops.attention_fwd(qs, ks, vs, causal=True)
+        ops.check()
+        assert torch.equal(os_, o[:, r * hp:(r + 1) * hp])
+
+
+def test_config4_full_b64():
+    """BASELINE config 4 as stated (B64 H16 N2048 d64, sigma 0.5) on one GPU:
+    16,384 work items.  Full tensor vs the scalar kernel, oracle rows on a
+    sample of (batch, head) planes."""
+    q, k, v = normal_inputs(64, 16, 16, 2048, 2048, 64, seed=6, sigma=0.5)
+    o = ops.attention_fwd(q, k, v)
+    s = ops.attention_fwd(q, k, v, scalar=True)
+    ops.check()
+    diff = (o.float() - s.float()).abs()
+    assert diff.max().item() <= 2e-2 and diff.mean().item() <= 2e-3, (diff.max(), diff.mean())
+    del s, diff
+    qh, kh, vh = to_host_bits(q), to_host_bits(k), to_host_bits(v)
+    oh = to_host_f32(o)
+    for b, h, r0 in ((0, 0, 0), (63, 15, 1920), (31, 7, 1000)):
+        ref = oracle.attention_rows(qh, kh, vh, b, h, h + 1, r0, r0 + 128)
+        gate(oh[b, h:h + 1, r0:r0 + 128], ref, f"rows b{b} h{h} r{r0}")
 
 
 def test_output_untouched_outside_tensor():
