@@ -443,8 +443,11 @@ b200_status b200_check(b200_stream_t stream) {
     const uint32_t zero = 0;
     e = cudaMemcpyToSymbol(b200::g_status, &zero, sizeof(zero));
     if (e != cudaSuccess) return cuda_fail(e, "clear status word");
-    return fail(B200_ETIMEOUT, "device wait timed out (status 0x%08x, site %u)", status,
-                (status >> 8) & 0xffu);
+    const uint32_t site = (status >> 8) & 0xffu;
+    if (site == b200::attn::kSiteSmemLayout)
+      return fail(B200_ECUDA, "attention kernel: dynamic shared memory starts too far past a "
+                  "1024-byte boundary for its tile layout (status 0x%08x)", status);
+    return fail(B200_ETIMEOUT, "device wait timed out (status 0x%08x, site %u)", status, site);
   }
   return B200_OK;
 }

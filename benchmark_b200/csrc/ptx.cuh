@@ -543,6 +543,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld_32x32b_x64(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+      : B200_R8(r, 0), B200_R8(r, 8), B200_R8(r, 16), B200_R8(r, 24), B200_R8(r, 32),
+        B200_R8(r, 40), B200_R8(r, 48), B200_R8(r, 56)
+      : "r"(taddr));
+}
+
 // 16-lane shapes: a warp reads or writes 16 TMEM lanes (rows) starting at
 // the lane in taddr (0 or 16 within its 32-lane sub-partition).
 //   16x256b.xN (ld): thread t holds rows t/4 and t/4+8, columns 8k+2(t%4) and
@@ -597,6 +605,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(
+          taddr),
+      B200_W8(r, 0)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
@@ -620,6 +636,17 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
                : B200_RW8(r, 0), B200_RW8(r, 8), B200_RW8(r, 16), B200_RW8(r, 24)
                :
                : "memory");
+}
+
+// No instruction: marks the 32 registers as written here.  Placed after a
+// tcgen05.wait::ld that covers their load, it keeps the compiler from moving
+// any use of them above that wait.
+__device__ __forceinline__ void reg_written_here(uint32_t (&r)[32]) {
+  asm volatile("" : B200_RW8(r, 0), B200_RW8(r, 8), B200_RW8(r, 16), B200_RW8(r, 24));
+}
+
+__device__ __forceinline__ void reg_written_here16(uint32_t (&r)[16]) {
+  asm volatile("" : B200_RW8(r, 0), B200_RW8(r, 8));
 }
 
 __device__ __forceinline__ void tmem_wait_st() {

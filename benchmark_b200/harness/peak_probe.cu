@@ -30,9 +30,10 @@ constexpr int kSmemProbe = 120 * 1024;  // keeps one CTA (and its 512 TMEM colum
 // (ts = 0), TMEM (ts = 1) or alternating (ts = 2: shared-A MMAs into one
 // accumulator, TMEM-A MMAs into another, the attention kernel's S/PV mix),
 // issued back to back by one warp.  accs = 2 alternates the accumulator
-// between columns [0, N) and [128, 128 + N) (N = 128 only).
+// between columns [0, N) and [128, 128 + N) (N = 128 only).  fill = 0: zero
+// operands; fill = 1: bf16 near 1.0 (the reference probe's fill).
 __global__ void __launch_bounds__(128, 1)
-    mma_probe(int n, int ts, int accs, int iters, unsigned long long* cycles) {
+    mma_probe(int n, int ts, int accs, int fill, int iters, unsigned long long* cycles) {
   extern __shared__ uint8_t raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -40,8 +41,9 @@ __global__ void __launch_bounds__(128, 1)
   uint8_t* b = smem + 16384;                 // 256 x 64 bf16, K-major SW128 (32 KiB)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 16384 + 32768);
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + 16384 + 32768 + 16);
-  for (int i = threadIdx.x; i < (16384 + 32768) / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  for (int i = threadIdx.x; i < (16384 + 32768) / 4; i += blockDim.x)
+    reinterpret_cast<uint32_t*>(smem)[i] =
+        fill ? 0x3f803f80u ^ (static_cast<uint32_t>(i) & 0x000f000fu) : 0u;
   fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     mbar_init(bar, 1);
@@ -141,14 +143,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
 // the same A and B descriptors for every MMA, the pattern of the reference's
 // issue-rate probe (1.mma/mma_throughput_bench.cu:404-460); reuse = 0 walks
 // four K slices of distinct operands, as a kernel's K loop does.  Operands
-// are bf16 near 1.0 (the reference probe's fill).
-__global__ void __launch_bounds__(128) mma_issue_probe(int issuers, int reuse, int iters,
-                                                       unsigned long long* cycles) {
+// are bf16 near 1.0 (fill = 1, the reference probe's fill) or zero (fill = 0).
+__global__ void __launch_bounds__(128) mma_issue_probe(int issuers, int reuse, int fill,
+                                                       int iters, unsigned long long* cycles) {
   __shared__ __align__(1024) uint8_t smem[32768];  // A 128x64 | B 128x64 (K-major SW128)
   __shared__ uint64_t bar;
   __shared__ uint32_t slot;
   for (int i = threadIdx.x; i < 32768 / 4; i += blockDim.x)
-    reinterpret_cast<uint32_t*>(smem)[i] = 0x3f803f80u ^ (static_cast<uint32_t>(i) & 0x000f000fu);
+    reinterpret_cast<uint32_t*>(smem)[i] =
+        fill ? 0x3f803f80u ^ (static_cast<uint32_t>(i) & 0x000f000fu) : 0u;
   fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     mbar_init(&bar, static_cast<uint32_t>(issuers));
@@ -347,15 +350,18 @@ int main(int argc, char** argv) {
     const int shapes[6][3] = {{256, 0, 1}, {128, 0, 1}, {128, 1, 1},
                               {128, 0, 2}, {128, 1, 2}, {128, 2, 2}};
     const char* src_name[3] = {"ss", "ts", "ss_ts"};
-    for (const auto& sh : shapes) {
-      const int n = sh[0], ts = sh[1], accs = sh[2];
-      const double ms = timed([&] {
-        mma_probe<<<sms, 128, kSmemProbe>>>(n, ts, accs, iters, cyc);
-      });
-      const double per_mma = mean_cycles(cyc, sms) / (4.0 * iters);
-      const double flops = 2.0 * 128 * n * 16 * 4.0 * iters * sms;
-      std::printf("probe=mma_m128_n%d_%s_%dacc cycles_per_mma=%.2f value=%.1f unit=TFLOP/s "
-                  "ms=%.4f\n", n, src_name[ts], accs, per_mma, flops / (ms * 1e-3) / 1e12, ms);
+    for (int fill = 0; fill < 2; ++fill) {
+      for (const auto& sh : shapes) {
+        const int n = sh[0], ts = sh[1], accs = sh[2];
+        const double ms = timed([&] {
+          mma_probe<<<sms, 128, kSmemProbe>>>(n, ts, accs, fill, iters, cyc);
+        });
+        const double per_mma = mean_cycles(cyc, sms) / (4.0 * iters);
+        const double flops = 2.0 * 128 * n * 16 * 4.0 * iters * sms;
+        std::printf("probe=mma_m128_n%d_%s_%dacc%s cycles_per_mma=%.2f value=%.1f "
+                    "unit=TFLOP/s ms=%.4f\n", n, src_name[ts], accs, fill ? "_ones" : "",
+                    per_mma, flops / (ms * 1e-3) / 1e12, ms);
+      }
     }
   }
   if (probe == "mma" || probe == "all") {
@@ -376,24 +382,28 @@ int main(int argc, char** argv) {
     // M128 N128 SS: issue warps per CTA x CTAs per SM (at most four 128-column
     // accumulators per SM), same or distinct operands.
     const int combos[6][2] = {{1, 1}, {2, 1}, {4, 1}, {1, 2}, {1, 4}, {2, 2}};
-    for (int reuse = 1; reuse >= 0; --reuse) {
-      for (const auto& c : combos) {
-        const int issuers = c[0], per_sm = c[1];
-        const int grid = sms * per_sm;
-        if (grid > 1024) continue;
-        const double ms = timed([&] {
-          mma_issue_probe<<<grid, 128>>>(issuers, reuse, iters, cyc);
-        });
-        unsigned long long h[1024];
-        cudaMemcpy(h, cyc, grid * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
-        unsigned long long mx = 0;
-        for (int i = 0; i < grid; ++i) mx = h[i] > mx ? h[i] : mx;
-        const double mmas_per_sm = 4.0 * iters * issuers * per_sm;
-        const double flops = 2.0 * 128 * 128 * 16 * mmas_per_sm * sms;
-        std::printf("probe=mma_m128_n128_ss_%s issuers_per_cta=%d ctas_per_sm=%d "
-                    "cycles_per_mma_per_sm=%.2f value=%.1f unit=TFLOP/s ms=%.4f\n",
-                    reuse ? "same_operands" : "distinct_operands", issuers, per_sm,
-                    static_cast<double>(mx) / mmas_per_sm, flops / (ms * 1e-3) / 1e12, ms);
+    for (int fill = 1; fill >= 0; --fill) {
+      for (int reuse = 1; reuse >= 0; --reuse) {
+        for (const auto& c : combos) {
+          const int issuers = c[0], per_sm = c[1];
+          const int grid = sms * per_sm;
+          if (grid > 1024) continue;
+          if (fill == 0 && (issuers != 1 || per_sm != 1)) continue;
+          const double ms = timed([&] {
+            mma_issue_probe<<<grid, 128>>>(issuers, reuse, fill, iters, cyc);
+          });
+          unsigned long long h[1024];
+          cudaMemcpy(h, cyc, grid * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+          unsigned long long mx = 0;
+          for (int i = 0; i < grid; ++i) mx = h[i] > mx ? h[i] : mx;
+          const double mmas_per_sm = 4.0 * iters * issuers * per_sm;
+          const double flops = 2.0 * 128 * 128 * 16 * mmas_per_sm * sms;
+          std::printf("probe=issue_m128_n128_ss_%s%s issuers_per_cta=%d ctas_per_sm=%d "
+                      "cycles_per_mma_per_sm=%.2f value=%.1f unit=TFLOP/s ms=%.4f\n",
+                      reuse ? "same_operands" : "distinct_operands", fill ? "" : "_zeros",
+                      issuers, per_sm, static_cast<double>(mx) / mmas_per_sm,
+                      flops / (ms * 1e-3) / 1e12, ms);
+        }
       }
     }
   }

@@ -61,13 +61,14 @@ b200_status attention_fwd(const void* q, const void* k, const void* v, void* o, 
 
 /*
  * attention_fwd with clock-cycle tracing of one CTA (diagnostics; runs the
- * default exp2 split).  trace: device buffer of 5 * trace_cap * 2 uint64
+ * default exp2 split).  trace: device buffer of 6 * trace_cap * 2 uint64
  * (zero it first).  Role r (0 Q/K TMA producer, 1 MMA issuer, 2 and 3 the
- * softmax warps 0 and 4, 4 epilogue) writes up to trace_cap records at
- * trace + r*trace_cap*2, each {(event << 32) | (tile << 24) | iteration,
- * clock64()}; softmax records carry the CTA's global K/V tile index as the
- * iteration.  Events are
- * listed in benchmark_b200/trace.py.  Stands in for the reference's
+ * softmax pipes 0 and 1 (their first warps), 4 epilogue, 5 V TMA producer)
+ * writes up to trace_cap records at trace + r*trace_cap*2, each
+ * {(event << 32) | (tile << 24) | iteration, clock64()}; the iteration of
+ * TMA, MMA and softmax records is the CTA's global K/V tile index.  Events
+ * are listed in benchmark_b200/trace.py, which also writes the reference's
+ * per-iteration trace CSV.  Stands in for the reference's
  * ATTENTION_CLOCK_TRACE build and its per-stage CSV
  * (0.attention/main.cu:175-272, 0.attention/main.cu:808-1157).
  */

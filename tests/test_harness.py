@@ -110,12 +110,13 @@ def test_peak_probe_all_runs_with_plausible_rates():
         if ln.startswith("probe="):
             kv = dict(x.split("=", 1) for x in ln.split() if "=" in x)
             vals[kv["probe"]] = float(kv["value"])
-    assert set(vals) == {"mma_m128_n256_ss_1acc", "mma_m128_n128_ss_1acc",
-                         "mma_m128_n128_ts_1acc", "mma_m128_n128_ss_2acc",
-                         "mma_m128_n128_ts_2acc", "mma_m128_n128_ss_ts_2acc",
-                         "mma_pair_m256_n128_ss", "mma_pair_m256_n256_ss",
-                         "tmem_ld_32x32b_x32", "tmem_st_32x32b_x32", "mufu_ex2_f32",
-                         "hbm_copy_1GiB"}
+    base = {"mma_m128_n256_ss_1acc", "mma_m128_n128_ss_1acc", "mma_m128_n128_ts_1acc",
+            "mma_m128_n128_ss_2acc", "mma_m128_n128_ts_2acc", "mma_m128_n128_ss_ts_2acc"}
+    assert set(vals) == base | {b + "_ones" for b in base} | {
+        "mma_pair_m256_n128_ss", "mma_pair_m256_n256_ss",
+        "issue_m128_n128_ss_same_operands", "issue_m128_n128_ss_distinct_operands",
+        "issue_m128_n128_ss_same_operands_zeros", "issue_m128_n128_ss_distinct_operands_zeros",
+        "tmem_ld_32x32b_x32", "tmem_st_32x32b_x32", "mufu_ex2_f32", "hbm_copy_1GiB"}
     assert vals["mma_m128_n256_ss_1acc"] > 500  # TFLOP/s
     assert vals["hbm_copy_1GiB"] > 1000        # GB/s
     assert all(v > 0 for v in vals.values())
