@@ -69,8 +69,17 @@ WORKLOADS = {
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel
 # of each workload, from the ncu captures summarised in profiles/ (None: not
-# captured).
-NCU_TRAFFIC_BYTES = {"c2": 515.99e6, "gemm": 1152.5e6}
+# captured).  c3 and c4 were captured on their 8-GPU shards (8 heads; batch 8)
+# and are scaled to the full problem by its items (the traffic grows with
+# them: each group of 8 planes, or each batch, streams its own K/V once).
+NCU_TRAFFIC_BYTES = {
+    "c2": 514.84e6,     # profiles/attention_fwd_d128_c2_b4h32n4096.md
+    "c1": 6.37e6,       # profiles/attention_fwd_d128_c1_b1h8n1024.md
+    "c3": 8 * 193.92e6,  # profiles/attention_fwd_d128_c3_causal_h8n16384.md
+    "c4": 8 * 110.97e6,  # profiles/attention_fwd_d64_c4_b8h16n2048.md
+    "gemm": 1152.5e6,   # profiles/gemm_bf16_pair_8192_b_row_major.md
+    "gemm16k": 20.78e9,  # profiles/gemm_bf16_pair_16384_b_col_major.md (B [N,K] capture)
+}
 
 L2_BYTES = 126 * 2**20
 

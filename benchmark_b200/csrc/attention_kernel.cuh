@@ -7,46 +7,52 @@
 // (attention.cu:167-174), ragged tails, head_dim 64 or 128.
 //
 // Persistent CTAs (one per SM) walk work items = (batch, q head, 128-row Q
-// tile).  Each item streams its head's K/V tiles (128 keys each).  The CTA's
-// K/V tiles form one global sequence t (crossing item boundaries); tile t
-// belongs to softmax pipe t & 1.  Each pipe keeps its own online-softmax state
-// (row max m, row sum l) and its own O accumulator for the item, and the
-// epilogue merges the two: O = (O0 2^(m0-m) + O1 2^(m1-m)) / (l0 2^(m0-m) +
-// l1 2^(m1-m)), m = max(m0, m1) -- the reference's two-pipe split
-// (attention.cu:1715-1947 merges its pipes the same way), here over a
-// persistent tile stream.  The two pipes' softmax warps share each scheduler
-// and run half a period apart, so one pipe's control latency (score load,
-// P publish, barrier waits) overlaps the other pipe's exp2 loop.  Roles:
+// tile).  Each item streams its head's K/V tiles (128 keys each).  Roles:
 //
-//   warps 0-3   softmax pipe 0, warps 4-7 softmax pipe 1: warp w owns TMEM
-//               lanes 32*(w%4) .. +32, one query row per thread, all 128
-//               keys of a tile in registers (no cross-thread reduction)
-//   warps 8-11  epilogue: merge O0/O1 -> bf16 -> shared -> TMA store
+//   warps 0-7   softmax: warp w owns 16 query rows (TMEM lanes
+//               32*(w%4) + 16*(w/4) + [0,16)), four threads per row
+//   warps 8-11  epilogue: O / l -> bf16 -> shared -> TMA store
 //   warp  12    TMA producer for Q (per item) and the K ring; TMEM allocator
 //   warp  13    tcgen05.mma issuer (whole warp, one elected lane issues)
-//   warp  14    TMA producer for the V ring
+//   warp  14    TMA producer for the V ring (its own thread, so K loads run
+//               ahead of the V ring's slower turnover)
 //   warp  15    idle; it completes warpgroup 3, so that each warpgroup can
 //               move its register budget with setmaxnreg (softmax 184,
 //               epilogue 56, producers/issuer 88 registers per thread)
 //
-// TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256, 256+D), O1
-// [256+D, 256+2D).  P(t) (bf16 pairs, key pair (2c, 2c+1) in column c)
-// overwrites the first 64 columns of its pipe's S buffer and is consumed by a
-// TS-MMA (A from TMEM).
+// TMEM (512 columns): three S buffers [0,128) [128,256) [256,384) rotate over
+// the global tile sequence; O at [384, 384+D).  P (bf16 pairs) overwrites the
+// first 64 columns of its S buffer; keys 0-63 land in columns [0,32), keys
+// 64-127 in [32,64).  The epilogue of an item reads O while the softmax
+// already works on the next item; the next item's first PV waits for it.
 //
-// MMA issue order over the tile stream: S(0), S(1), then for every t:
-// PV(t), S(t+2).  S(t+2) overwrites P(t) of the same pipe after PV(t) in
-// issue order (the tensor pipe executes one thread's MMAs in order), and the
-// commit that publishes S(t) also covers PV(t-2), so a softmax warp that
-// sees S(t) may rescale its pipe's O rows without another wait.
+// Why this shape: the tensor core runs M=128 products at full rate only for
+// N >= 128 with one operand in TMEM or both streams within the 128 B/clk
+// shared-memory read budget, and MUFU exp2 (16/clk/SM) costs as many cycles
+// per K/V tile as the two 128x128x128 products.  Three S buffers let S(t+1)
+// and S(t+2) run while the softmax of tile t runs, so neither the tensor core
+// nor the softmax waits on the other's latency and softmax warps may drift a
+// tile apart; eight independent softmax warps (16 rows each) put two on
+// every scheduler without any cross-warp barrier.
 //
-// Softmax per tile (one row per thread): the row max is thread-local (64
-// three-input max instructions, no shuffles), taken before the exp2 loop.  O
-// and the row sums are rescaled only when a tile raises the running max m by
-// more than kRescaleLog2 (otherwise P values up to 2^kRescaleLog2 accumulate
-// unscaled: exact in fp32, O / l unchanged).  Masked tiles (causal edge,
-// ragged tail) put the masked keys at -inf and use MUFU exp2 only (exact
-// zeros).
+// MMA issue order over the global tile stream t (crossing item boundaries):
+//   S(0), S(1), then for every t: S(t+2), PV(t)   (PV(t) issued once all
+//   eight softmax warps have stored P(t)).  S(t+3) overwrites P(t) after
+//   PV(t) in issue order; the tensor pipe executes one thread's MMAs in
+//   issue order.
+//
+// Softmax per tile: a thread reads 32 scores of each of its two rows
+// (16x256b TMEM loads); where a row max is needed it is completed by two
+// shuffles, and the running max m is kept in log2 units.  O and the row sums
+// are rescaled only when a block raises m by more than kRescaleLog2
+// (otherwise P values up to 2^kRescaleLog2 accumulate unscaled: exact in
+// fp32, O / l unchanged), after PV(t-1) has completed.  Unmasked tiles after
+// an item's first compute P against the running max directly and take the
+// tile max only when the P sums show a jump (rare).  P is stored with
+// 16x128b stores, whose column order matches the key pairs each thread
+// holds, and published (store wait, fence, one arrive per warp) at the end
+// of its own tile, before the next tile's scores are loaded: a TMEM store
+// wait or fence behind an outstanding TMEM load waits for that load too.
 //
 // Every wait is bounded (ptx.cuh).  A timeout sets the device status word;
 // the epilogue warps, which meet at a named barrier, agree on aborting
@@ -61,7 +67,6 @@ namespace attn {
 
 constexpr int kBM = 128;  // query rows per work item (= TMEM lanes)
 constexpr int kBN = 128;  // keys per K/V tile
-constexpr int kPipes = 2;
 constexpr int kEpiWarp0 = 8;
 constexpr int kTmaWarp = 12;   // Q and K loads
 constexpr int kMmaWarp = 13;
@@ -83,6 +88,7 @@ static_assert(kSoftmaxRegs % 8 == 0 && kEpiRegs % 8 == 0 && kCtlRegs % 8 == 0 &&
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
 constexpr float kRescaleP = 256.0f;  // 2^kRescaleLog2
+constexpr int kSBufs = 3;  // S buffers in TMEM (P overwrites its S buffer)
 constexpr int kBarEpilogue = 1;  // named barrier: warps 8-11
 
 struct Params {
@@ -92,11 +98,13 @@ struct Params {
   int n_items;   // B * Hq * n_qtiles
   int causal;      // bottom-right aligned
   int causal_off;  // Skv - Sq
+  int cgroup;      // causal: Q planes per ordering group (their K/V fit in L2 together)
+  int kv_evict_first;  // L2 policy of the K/V loads: 1 evict_first, 0 evict_last
   float scale_log2;  // softmax_scale * log2(e)
   // Clock trace (kTrace instantiations only): per-role record regions of
   // trace_cap records (2 x u64: (event << 32 | tile << 24 | iter), clock64)
-  // for CTA trace_cta.  Role r (0 Q/K TMA, 1 MMA, 2/3 softmax pipes 0/1, 4
-  // epilogue, 5 V TMA) starts at trace + r * trace_cap * 2.
+  // for CTA trace_cta.  Role r (0 Q/K TMA, 1 MMA, 2/3 softmax warps 0 and 4,
+  // 4 epilogue, 5 V TMA) starts at trace + r * trace_cap * 2.
   unsigned long long* trace;
   int trace_cap;
   int trace_cta;
@@ -108,7 +116,7 @@ enum : uint32_t {
   kEvSmReady, kEvSmLdDone, kEvSmMaxDone, kEvSmPComputed, kEvSmPublished, kEvSmItemEnd,
   kEvEpiBegin, kEvEpiEnd
 };
-constexpr int kTraceRoles = 6;  // 0 K/Q TMA, 1 MMA, 2/3 softmax pipes 0/1, 4 epilogue, 5 V TMA
+constexpr int kTraceRoles = 6;  // 0 K/Q TMA, 1 MMA, 2/3 softmax warps 0/4, 4 epilogue, 5 V TMA
 
 template <bool kTrace>
 struct Tracer {
@@ -141,45 +149,28 @@ struct Cfg {
   static constexpr int kTileBytes = kBoxes * kBoxBytes;
   static constexpr int kKStages = (D == 128) ? 3 : 4;  // K ring depth
   static constexpr int kVStages = (D == 128) ? 2 : 4;  // V ring depth
-  // Small objects first, at the (16-byte aligned) start of dynamic shared
-  // memory; the tile region follows at the next 1024-byte boundary (128-byte
-  // swizzled TMA boxes need it).  Per-row (m, l) of each pipe for the item
-  // the epilogue works on: [pipe][row] float2 (one slot suffices: the softmax
-  // writes item li's values only after the epilogue has released item li-1).
-  static constexpr int kStatOff = 0;
-  static constexpr int kFlagOff = kStatOff + kPipes * 128 * 8;  // abort flag (epilogue)
-  static constexpr int kBarOff = kFlagOff + 16;
-  // q_full[2] q_empty[2] k_full[K] k_empty[K] v_full[V] v_empty[V]
-  // s_ready[2] p_ready[2] o_full o_empty l_ready[2] drain done
-  static constexpr int kNumBars = 4 + 2 * kKStages + 2 * kVStages + 2 * kPipes + 2 + 2 + 2;
-  static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
-  static constexpr int kSmallBytes = (kTmemSlotOff + 16 + 15) / 16 * 16;
-  // Tile region, relative to its 1024-byte aligned start.
-  static constexpr int kQOff = 0;  // Q0, Q1 (also O staging)
+  static constexpr int kQOff = 0;                       // Q0, Q1 (also O staging)
   static constexpr int kKOff = 2 * kTileBytes;
   static constexpr int kVOff = kKOff + kKStages * kTileBytes;
-  static constexpr int kTileRegion = kVOff + kVStages * kTileBytes;
-  // With the d=128 rings the whole budget is needed: the request is the
-  // 227 KiB a CTA may use, which holds the layout whenever dynamic shared
-  // memory starts at most 1024 - (kSmallBytes % 1024) bytes past a 1024-byte
-  // boundary (it starts on one); the kernel checks and reports otherwise.
-  static constexpr int kSmemMax = 232448;
-  static constexpr int kSmemBytes = kSmallBytes + 1024 + kTileRegion <= kSmemMax
-                                        ? kSmallBytes + 1024 + kTileRegion
-                                        : kSmemMax;
-  static_assert(kSmallBytes + kTileRegion + (1024 - kSmallBytes % 1024) % 1024 <= kSmemMax,
-                "exceeds the 227 KiB of shared memory a CTA may use");
+  static constexpr int kLOff = kVOff + kVStages * kTileBytes;  // row sums [2 items][128]
+  static constexpr int kFlagOff = kLOff + 2 * 128 * 4;        // abort flag (epilogue)
+  static constexpr int kBarOff = kFlagOff + 16;
+  // q_full[2] q_empty[2] k_full[K] k_empty[K] v_full[V] v_empty[V]
+  // s_ready[3] p_ready[3] pv_done o_full o_empty l_ready[2] drain done
+  static constexpr int kNumBars = 4 + 2 * kKStages + 2 * kVStages + 2 * kSBufs + 1 + 4 + 2;
+  static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
+  static constexpr int kSmemBytes = kTmemSlotOff + 16 + 1024;  // + 1 KiB alignment slack
+  static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB of shared memory a CTA may use");
   static constexpr uint32_t kIdescS = idesc_bf16_f32(128, kBN, false, false);
   static constexpr uint32_t kIdescO = idesc_bf16_f32(128, D, false, true);
-  static constexpr uint32_t kColO = 128 * kPipes;  // O0 at kColO, O1 at kColO + D
-  static_assert(kColO + kPipes * D <= kTmemCols, "TMEM budget");
+  static constexpr uint32_t kColO = 128 * kSBufs;
 };
 
 // Wait sites reported in the status word.
 enum : uint32_t {
   kSiteQFull = 1, kSiteKFull, kSiteVFull, kSitePReady, kSiteKEmpty, kSiteVEmpty,
   kSiteSReady, kSiteOFull, kSiteQEmpty, kSitePvDone, kSiteOEmpty, kSiteLReady,
-  kSiteSmemLayout = 0xF0  // the tile region did not fit behind the small objects
+  kSiteSmemLayout = 0xF0  // reserved: a tile layout that does not fit its shared memory
 };
 
 // Number of K/V tiles the Q tile at `tile_row0` must visit (0 if it has no
@@ -206,14 +197,19 @@ struct Item {
 };
 
 // Work item k.  Non-causal: items of one head are adjacent, so the CTAs
-// running at one time share a few heads' K/V in L2.  Causal: the heaviest Q
-// tiles (last rows) come first.
+// running at one time share a few heads' K/V in L2.  Causal: planes are taken
+// in groups of p.cgroup (sized on the host so that a group's K/V fit in L2
+// together); inside a group the heaviest Q tiles (last rows) come first.
 __device__ __forceinline__ Item decode_item(const Params& p, int k) {
   const int bhs = p.B * p.Hq;
   int bh, qt;
   if (p.causal) {
-    qt = p.n_qtiles - 1 - k / bhs;
-    bh = k - (k / bhs) * bhs;
+    const int per_group = p.cgroup * p.n_qtiles;
+    const int g = k / per_group;
+    const int kl = k - g * per_group;
+    const int gs = min(p.cgroup, bhs - g * p.cgroup);  // planes in this group
+    qt = p.n_qtiles - 1 - kl / gs;
+    bh = g * p.cgroup + (kl - (kl / gs) * gs);
   } else {
     bh = k / p.n_qtiles;
     qt = k - bh * p.n_qtiles;
@@ -254,60 +250,39 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// P for keys [16c, 16c+16) of this thread's row (s: those 16 scores):
-// exp2(s * sc + nm) as 8 bf16 pairs (pk[i] = keys 2i, 2i+1), accumulating
-// the fp32 row sum in two packed pairs.  kEmu of every 8 pairs use the
-// FMA-pipe exp2 (exp2_fma_x2).  Masked tiles: keys at or past `va` (counted
-// from this chunk's first key) get exactly 0 (MUFU of -inf).
+// P for 32 keys of each of this thread's two rows (8 repeats of the
+// 16x256b layout: s[4g], s[4g+1] row a, s[4g+2], s[4g+3] row b): exp2(x) as
+// bf16 pairs, x = s * sc - m (s pre-scaled in masked blocks, sc = 1); pk[2g]
+// row a, pk[2g+1] row b (the 16x128b store order).  Accumulates fp32 row
+// sums in packed pairs.  kEmu of every 8 pairs use the FMA-pipe exp2
+// (exp2_fma_x2), the rest MUFU; masked blocks use MUFU only (exact zeros).
 template <int kEmu, bool kMasked>
-__device__ __forceinline__ void p_chunk(const float* s, uint64_t sc2, uint64_t nm2, int va,
-                                        uint64_t& ra, uint64_t& rb, uint32_t (&pk)[8]) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint64_t x2 = f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sc2, nm2);
-    float x0, x1, p0, p1;
-    f2_unpack(x2, x0, x1);
-    if (kMasked) {
-      x0 = 2 * i < va ? x0 : -INFINITY;
-      x1 = 2 * i + 1 < va ? x1 : -INFINITY;
-    }
-    if (!kMasked && i < kEmu) {
-      exp2_fma_x2(x0, x1, p0, p1);
-    } else {
-      p0 = ex2_approx(x0);
-      p1 = ex2_approx(x1);
-    }
-    if (i & 1)
-      rb = f2_add(rb, f2_pack(p0, p1));
-    else
-      ra = f2_add(ra, f2_pack(p0, p1));
-    pk[i] = pack_bf16x2(p0, p1);
-  }
-}
-
-// P of a whole 128-key tile row, stored over the first 64 columns of the
-// pipe's S buffer (tS: this thread's lane, column 0).
-template <int kEmu, bool kMasked>
-__device__ __forceinline__ void p_tile(const float* s, float sc, float nm, int va, uint32_t tS,
-                                       uint64_t& ra, uint64_t& rb) {
+__device__ __forceinline__ void p_rows(const float* s, float sc, float nm_a, float nm_b,
+                                       uint64_t& rs_a, uint64_t& rs_b, uint32_t (&pk)[16]) {
   const uint64_t sc2 = f2_pack(sc, sc);
-  const uint64_t nm2 = f2_pack(nm, nm);
+  const uint64_t na2 = f2_pack(nm_a, nm_a);
+  const uint64_t nb2 = f2_pack(nm_b, nm_b);
 #pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    uint32_t pk[8];
-    p_chunk<kEmu, kMasked>(s + 16 * c, sc2, nm2, va - 16 * c, ra, rb, pk);
-    tmem_st8(tS + 8 * c, pk);
+  for (int g = 0; g < 8; ++g) {
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint64_t x2 = f2_fma(f2_pack(s[4 * g + 2 * rr], s[4 * g + 2 * rr + 1]), sc2,
+                                 rr ? nb2 : na2);
+      float x0, x1, p0, p1;
+      f2_unpack(x2, x0, x1);
+      if (!kMasked && ((2 * g + rr) & 7) < kEmu) {
+        exp2_fma_x2(x0, x1, p0, p1);
+      } else {
+        p0 = ex2_approx(x0);
+        p1 = ex2_approx(x1);
+      }
+      if (rr)
+        rs_b = f2_add(rs_b, f2_pack(p0, p1));
+      else
+        rs_a = f2_add(rs_a, f2_pack(p0, p1));
+      pk[2 * g + rr] = pack_bf16x2(p0, p1);
+    }
   }
-}
-
-// Largest of a row's 128 scores (four independent chains).
-__device__ __forceinline__ float row_max128(const float* s) {
-  float a[4];
-#pragma unroll
-  for (int u = 0; u < 4; ++u) a[u] = fmaxf(s[2 * u], s[2 * u + 1]);
-#pragma unroll
-  for (int g = 4; g < 64; ++g) a[g & 3] = fmax3(a[g & 3], s[2 * g], s[2 * g + 1]);
-  return fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3]));
 }
 
 template <int D, int kEmu, bool kTrace = false>
@@ -318,20 +293,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                          const __grid_constant__ CUtensorMap o_map, const Params p) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* tiles = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw + C::kSmallBytes) + 1023) &
-      ~static_cast<uintptr_t>(1023));
-  if (tiles + C::kTileRegion > smem_raw + C::kSmemBytes) {
-    // Uniform across the CTA, before any barrier or TMEM use.
-    if (threadIdx.x == 0) report_timeout(kSiteSmemLayout);
-    return;
-  }
-  uint8_t* q_buf = tiles + C::kQOff;
-  uint8_t* k_buf = tiles + C::kKOff;
-  uint8_t* v_buf = tiles + C::kVOff;
-  float2* stat = reinterpret_cast<float2*>(smem_raw + C::kStatOff);  // [pipe][row] = (m, l)
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem_raw + C::kFlagOff);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + C::kBarOff);
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* q_buf = smem + C::kQOff;
+  uint8_t* k_buf = smem + C::kKOff;
+  uint8_t* v_buf = smem + C::kVOff;
+  float* lsum = reinterpret_cast<float*>(smem + C::kLOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kFlagOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* q_full = bars;
   uint64_t* q_empty = q_full + 2;
   uint64_t* k_full = q_empty + 2;
@@ -339,13 +308,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_full = k_empty + C::kKStages;
   uint64_t* v_empty = v_full + C::kVStages;
   uint64_t* s_ready = v_empty + C::kVStages;
-  uint64_t* p_ready = s_ready + kPipes;
-  uint64_t* o_full = p_ready + kPipes;
+  uint64_t* p_ready = s_ready + kSBufs;
+  uint64_t* pv_done = p_ready + kSBufs;
+  uint64_t* o_full = pv_done + 1;
   uint64_t* o_empty = o_full + 1;
   uint64_t* l_ready = o_empty + 1;
   uint64_t* drain = l_ready + 2;
   uint64_t* done = drain + 1;  // phase 0 completes at setup and never changes
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + C::kTmemSlotOff);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmemSlotOff);
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -356,11 +326,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
-      mbar_init(&l_ready[i], 8);  // all eight softmax warps
+      mbar_init(&l_ready[i], 8);
     }
-    for (int i = 0; i < kPipes; ++i) {
+    for (int i = 0; i < kSBufs; ++i) {
       mbar_init(&s_ready[i], 1);
-      mbar_init(&p_ready[i], 4);  // the pipe's four softmax warps
+      mbar_init(&p_ready[i], 8);
     }
     mbar_init(o_full, 1);
     mbar_init(o_empty, 128);
@@ -372,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
+    mbar_init(pv_done, 1);
     mbar_init(drain, 1);
     mbar_init(done, 1);
     mbar_arrive(done);
@@ -404,7 +375,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool is_k = warp == kTmaWarp;
         Tracer<kTrace> tr(p, is_k ? 0 : 5, trace_cta);
         const uint64_t pol_q = l2_policy_evict_first();
-        const uint64_t pol_kv = l2_policy_evict_last();
+        const uint64_t pol_kv =
+            p.kv_evict_first ? l2_policy_evict_first() : l2_policy_evict_last();
         int t = 0, li = 0, issued = 0, q_issued = -1;
         bool ok = true;
         for (int r = 0; r < rounds && ok; ++r) {
@@ -480,6 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t dk0 = sdesc_sw128(k_addr, 16, 1024);
         const uint64_t dv0 = sdesc_sw128(v_addr, C::kBoxBytes, 1024);
         constexpr uint32_t kTile16 = C::kTileBytes >> 4, kBox16 = C::kBoxBytes >> 4;
+        const uint32_t tO = tmem_base + C::kColO;
         // Filler for unused slots of the grouped waits.
         const uint32_t dn_a = smem_u32(done), dn_p = 0;
         auto bar = [](uint64_t* b_) { return smem_u32(b_); };
@@ -493,31 +466,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           tr(kEvMmaGo, site, 0);
           return true;
         };
-        // S(t) = Q[qb] K(t)^T into pipe (t & 1)'s S buffer.
+        // S(t) = Q[qb] K(t)^T into S buffer t % kSBufs.
         auto issue_s = [&](int t_, int qb) {
           tr(kEvMmaS, qb, t_);
           const uint64_t dq = dq0 + qb * kTile16;
           const uint64_t dk = dk0 + (t_ % C::kKStages) * kTile16;
-          const uint32_t ts = tmem_base + static_cast<uint32_t>((t_ & 1) * 128);
-#pragma unroll
+          const uint32_t ts = tmem_base + static_cast<uint32_t>((t_ % kSBufs) * 128);
+  #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * kBox16 + (kk & 3) * 2;
             mma_ss_warp(ts, dq + off, dk + off, C::kIdescS, kk > 0 ? 1u : 0u);
           }
           mma_commit_warp(&k_empty[t_ % C::kKStages]);
-          mma_commit_warp(&s_ready[t_ & 1]);
+          mma_commit_warp(&s_ready[t_ % kSBufs]);
         };
-        // O[pipe] (+)= P(t) V(t); `first`: the pipe's first tile of the item
-        // overwrites O.
-        auto issue_pv = [&](int t_, bool first) {
-          tr(kEvMmaPv, t_ & 1, t_);
+        // O (+)= P(t)[keys 64*half ...] V(t)[keys 64*half ...]
+        auto issue_pv_half = [&](int t_, bool first, int half) {
+          if (half == 0) tr(kEvMmaPv, 0, t_);
           const uint64_t dv = dv0 + (t_ % C::kVStages) * kTile16;
-          const uint32_t tp = tmem_base + static_cast<uint32_t>((t_ & 1) * 128);
-          const uint32_t to = tmem_base + C::kColO + static_cast<uint32_t>((t_ & 1) * D);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ts_warp(to, tp + kk * 8, dv + kk * (2048 >> 4), C::kIdescO,
+          const uint32_t tp = tmem_base + static_cast<uint32_t>((t_ % kSBufs) * 128);
+  #pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const int kk = half * 4 + k4;
+            mma_ts_warp(tO, tp + kk * 8, dv + kk * (2048 >> 4), C::kIdescO,
                         (!first || kk > 0) ? 1u : 0u);
+          }
         };
         // Next valid round after r (rounds if none).
         auto next_round = [&](int r) {
@@ -526,8 +499,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           return r;
         };
 
-        // S cursor: the next S to issue, at most two tiles ahead of the PV
-        // cursor (S(t+2) reuses PV(t)'s P buffer).
+        // S cursor: the next S to issue, up to kSBufs - 1 tiles ahead of the
+        // PV cursor and never beyond the item after the PV cursor's (the Q of
+        // a later item waits for an epilogue that waits for this thread).
         int s_r = next_round(-1), s_li = 0, s_j = 0, s_t = 0;
         Item s_it{};
         auto s_settle = [&]() {  // move past items without K/V tiles
@@ -539,8 +513,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         };
         s_settle();
-        auto issue_s_upto = [&](int limit_t) -> bool {
-          while (s_r < rounds && s_t <= limit_t) {
+        auto issue_s_upto = [&](int limit_t, int max_li) -> bool {
+          while (s_r < rounds && s_t <= limit_t && s_li <= max_li) {
             const int qb = s_li & 1;
             if (s_j == 0 &&
                 !wait3(bar(&q_full[qb]), static_cast<uint32_t>(s_li >> 1) & 1u, dn_a, dn_p, dn_a,
@@ -563,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
         // PV cursor.
         int t = 0, li = 0;
-        bool ok = issue_s_upto(1);
+        bool ok = true;
         for (int r = next_round(-1); r < rounds && ok; r = next_round(r), ++li) {
           const Item it = decode_item(p, item_index(p, r));
           const uint32_t oe_par = (static_cast<uint32_t>(li) & 1u) ^ 1u;  // epilogue of li-1
@@ -578,18 +552,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           for (int j = 0; j < it.n && ok; ++j) {
             const int tt = t + j;
-            // Both O accumulators are free once the epilogue of item li-1 has
-            // read them (the other pipe's first PV comes after this one).
-            ok = wait3(bar(&v_full[tt % C::kVStages]), vpar(tt), bar(&p_ready[tt & 1]),
-                       static_cast<uint32_t>(tt >> 1) & 1u, j == 0 ? bar(o_empty) : dn_a,
-                       j == 0 ? oe_par : dn_p, kSitePReady);
+            const uint32_t tpar = static_cast<uint32_t>(tt / kSBufs) & 1u;
+            ok = issue_s_upto(tt + kSBufs - 1, li + 1);
             if (!ok) break;
-            issue_pv(tt, j < 2);
+            if (j == 0) {
+              // O is free once the epilogue of item li-1 has read it.
+              ok = wait3(bar(o_empty), oe_par, dn_a, dn_p, dn_a, dn_p, kSiteOEmpty);
+              if (!ok) break;
+            }
+            // One grouped wait per PV: polls cost a few hundred cycles each,
+            // and S(t+2), issued just before, keeps the tensor pipe busy
+            // meanwhile.
+            ok = wait3(bar(&v_full[tt % C::kVStages]), vpar(tt), bar(&p_ready[tt % kSBufs]), tpar,
+                       dn_a, dn_p, kSitePReady);
+            if (!ok) break;
+            issue_pv_half(tt, j == 0, 0);
+            issue_pv_half(tt, j == 0, 1);
             mma_commit_warp(&v_empty[tt % C::kVStages]);
-            if (j == it.n - 1) mma_commit_warp(o_full);
-            ok = issue_s_upto(tt + 2);
+            mma_commit_warp(pv_done);
           }
           if (!ok) break;
+          mma_commit_warp(o_full);
           t += it.n;
         }
         // Every MMA issued above has completed once this commit lands.
@@ -602,31 +585,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < static_cast<uint32_t>(kEpiWarp0)) {
     setmaxnreg_inc<kSoftmaxRegs>();
     // ================= softmax (warps 0-7) =================
-    // Pipe `pipe` handles the tiles t with (t & 1) == pipe.  Thread `lane`
-    // of warp w owns query row 32*(w%4) + lane of the item.
-    const int pipe = static_cast<int>(warp >> 2);
+    // Warp w owns 16 rows: TMEM lanes 32*(w%4) + 16*(w/4) + [0,16).  Thread
+    // t of the warp holds rows t/4 and t/4+8 and, of every 8 keys, the pair
+    // 2*(t%4), 2*(t%4)+1 (16x256b loads); that pair is one packed P column
+    // (16x128b stores), and a row's max needs only two shuffles among the
+    // four threads that share it.
     const uint32_t quad = warp & 3u;
-    const int row = static_cast<int>(quad * 32 + lane);
-    const uint32_t lane_addr = (quad * 32u) << 16;
-    const uint32_t tS = tmem_base + lane_addr + static_cast<uint32_t>(pipe * 128);
-    const uint32_t tO = tmem_base + lane_addr + C::kColO + static_cast<uint32_t>(pipe * D);
+    const int rbase = static_cast<int>(quad * 32 + (warp >> 2) * 16);
+    const int t0 = static_cast<int>(lane & 3u);
+    const int ra = rbase + static_cast<int>(lane >> 2);  // rows of this thread
+    const int rb = ra + 8;
+    const uint32_t lane_addr = static_cast<uint32_t>(rbase) << 16;
     const float c = p.scale_log2;
-    Tracer<kTrace> tr(p, 2 + pipe, trace_cta && quad == 0 && lane == 0);
+    Tracer<kTrace> tr(p, 2 + static_cast<int>(warp >> 2), trace_cta && quad == 0 && lane == 0);
     int t = 0, li = 0;
     bool ok = true;
-    // Multiply this pipe's O rows by f (rare; f = 1 for rows that did not
-    // move).  PV(t-2) of this pipe has completed: the commit that published
-    // S(t) covers it.
-    auto rescale_o = [&](float f) {
-#pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 16) {
-        uint32_t o[16];
-        tmem_ld16(tO + c0, o);
-        tmem_wait_ld();
-        reg_written_here16(o);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-        tmem_st16(tO + c0, o);
+    // K/V tiles this CTA processes in all (the global tile sequence t).
+    int g_total = 0;
+    for (int r = 0; r < rounds; ++r) {
+      const int k = item_index(p, r);
+      if (k < p.n_items) g_total += decode_item(p, k).n;
+    }
+    // S(tt) lives in sr once loaded; the load of its successor in the global
+    // tile sequence (also across an item boundary) is issued as soon as tile
+    // tt's P is computed, so its latency overlaps the P stores and the
+    // bookkeeping.
+    uint32_t sr[64];
+    bool have_s = false;
+    // One 16x256b.x16 load of a tile's scores for d=128; two x8 loads (keys
+    // 0-63, then 64-127) for d=64 (same registers; measured +3.4 % on d=64
+    // and -5 % on d=128).
+    auto load_s = [&](uint32_t taddr) {
+      if constexpr (D == 64) {
+        tmem_ld_16x256b_x8(taddr, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tmem_ld_16x256b_x8(taddr + 64u, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      } else {
+        tmem_ld_16x256b_x16(taddr, sr);
       }
     };
 #pragma unroll 1
@@ -635,88 +629,256 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (k >= p.n_items) continue;
       const Item it = decode_item(p, k);
       const int qb = li & 1;
-      const int lim = p.causal ? min(p.Skv, it.row0 + row + p.causal_off + 1) : p.Skv;
-      // Running max of scaled scores (log2 units) and the row sum (two
-      // packed pairs) of this pipe for the item.
-      float m = -INFINITY;
-      float l = 0.0f;
+      const uint32_t tO = tmem_base + lane_addr + C::kColO;
+      const int lim_a = p.causal ? min(p.Skv, it.row0 + ra + p.causal_off + 1) : p.Skv;
+      const int lim_b = p.causal ? min(p.Skv, it.row0 + rb + p.causal_off + 1) : p.Skv;
+      // Running max of scaled scores (log2 units) and this thread's share of
+      // the row sums, for rows a and b.
+      float m_a = -INFINITY, m_b = -INFINITY;
+      uint64_t l2_a = 0ull, l2_b = 0ull;  // packed pairs: even and odd keys
+      bool all_finite = false;  // every row of this warp has a finite running max
 #pragma unroll 1
-      for (int j = ((t & 1) == pipe) ? 0 : 1; j < it.n; j += 2) {
+      for (int j = 0; j < it.n; ++j) {
         const int tt = t + j;
-        tr(kEvSmWait, pipe, tt);
-        ok = warp_wait(&s_ready[pipe], static_cast<uint32_t>(tt >> 1) & 1u, kSiteSReady);
-        if (!ok) break;
-        tr(kEvSmReady, pipe, tt);
-        tc_fence_after();
-        uint32_t sr[128];
-        tmem_ld_32x32b_x64(tS, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
-        tmem_ld_32x32b_x64(tS + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
+        const int sb = tt % kSBufs;
+        const uint32_t tS = tmem_base + lane_addr + static_cast<uint32_t>(sb * 128);
+        tr(kEvSmWait, warp >> 2, tt);
+        if (!have_s) {
+          ok = warp_wait(&s_ready[sb], static_cast<uint32_t>(tt / kSBufs) & 1u, kSiteSReady);
+          if (!ok) break;
+          tc_fence_after();
+          load_s(tS);
+        }
+        tr(kEvSmReady, warp >> 2, tt);
         tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-        reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-        reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
-        reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
-        tr(kEvSmLdDone, pipe, tt);
+        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        have_s = false;
+        tr(kEvSmLdDone, warp >> 2, tt);
         float* s = reinterpret_cast<float*>(sr);
         const int kbase = j * kBN;
-        const bool masked = kbase + kBN > it.min_lim;  // uniform across the CTA
-        const bool first = j < 2;  // this pipe's first tile of the item: its PV overwrites O
-        // Exact row max (thread-local: the thread holds its whole row), then
-        // the running-max update with lazy rescaling.
-        // Valid keys of this row in the tile (masked tiles only).
-        const int va = lim - kbase;
-        float mx;
-        if (masked) {
-          float a4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        const bool masked = kbase + kBN > it.min_lim;  // uniform across the tile
+        float f_a = 1.0f, f_b = 1.0f;
+        bool rescale = false;    // this thread's rows
+        uint64_t rs_a = 0ull, rs_b = 0ull;
+        // Readiness of S(tt+1), tested right after this tile's P loop so that
+        // the test's latency overlaps the work that follows.
+        const int nb = (tt + 1) % kSBufs;
+        bool ready = false;      // this lane's test
+        bool ready_all = false;  // the warp's vote on it
+        // Rescale the O rows whose maximum jumped, once PV(tt-1) has
+        // completed (PV(tt) waits for this tile's P barrier); rare.
+        auto rescale_o = [&]() {
+          if (!warp_wait(pv_done, static_cast<uint32_t>(tt - 1) & 1u, kSitePvDone)) {
+            ok = false;
+            return;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c0 = 0; c0 < D; c0 += 64) {
+            uint32_t o[32];
+            tmem_ld_16x256b_x8(tO + c0, o);
+            tmem_wait_ld(o);
 #pragma unroll
-          for (int i = 0; i < 128; ++i) a4[i & 3] = i < va ? fmaxf(a4[i & 3], s[i]) : a4[i & 3];
-          const float smax = fmaxf(fmaxf(a4[0], a4[1]), fmaxf(a4[2], a4[3]));
-          mx = smax == -INFINITY ? -INFINITY : smax * c;  // no valid key: stays -inf
+            for (int g = 0; g < 8; ++g) {
+              o[4 * g + 0] = __float_as_uint(__uint_as_float(o[4 * g + 0]) * f_a);
+              o[4 * g + 1] = __float_as_uint(__uint_as_float(o[4 * g + 1]) * f_a);
+              o[4 * g + 2] = __float_as_uint(__uint_as_float(o[4 * g + 2]) * f_b);
+              o[4 * g + 3] = __float_as_uint(__uint_as_float(o[4 * g + 3]) * f_b);
+            }
+            tmem_st_16x256b_x8(tO + c0, o);
+          }
+        };
+        // A later unmasked tile of rows that already have a finite running max
+        // computes P against that max at once, without the tile max; only
+        // when some row's max rose by more than 2^kRescaleLog2 (rare, screened
+        // by the P sums) is the max taken and P recomputed against it.  Same
+        // results as taking the max first: m only moves when the block raises
+        // it past the threshold, and then to the block max.
+        const bool spec = !masked && j > 0 && all_finite;
+        if (spec) {
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t pk[16];
+            p_rows<kEmu, false>(s + 32 * half, c, -m_a, -m_b, rs_a, rs_b, pk);
+            tmem_st_16x128b_x8(tS + 32 * half, pk);
+          }
+          ready = mbar_try_wait(smem_u32(&s_ready[nb]), static_cast<uint32_t>((tt + 1) / kSBufs) & 1u);
+          tr(kEvSmMaxDone, warp >> 2, tt);
+          // Some x of the tile exceeds kRescaleLog2 only if some P value
+          // exceeds kRescaleP, and then so does the sum of its lane (all terms
+          // are non-negative): the partial sums screen for the rare case, and
+          // only then are the exact maxima taken.
+          float q0, q1, q2, q3;
+          f2_unpack(rs_a, q0, q1);
+          f2_unpack(rs_b, q2, q3);
+          const bool big = __any_sync(0xffffffffu, fmaxf(fmaxf(q0, q1), fmaxf(q2, q3)) > kRescaleP);
+          // Both votes in flight before the first branch on either.
+          ready_all = __all_sync(0xffffffffu, ready);
+          if (big) {
+            float ma = -INFINITY, mb = -INFINITY;
+#pragma unroll
+            for (int g = 0; g < 16; ++g) {
+              ma = fmax3(ma, s[4 * g], s[4 * g + 1]);
+              mb = fmax3(mb, s[4 * g + 2], s[4 * g + 3]);
+            }
+            // fma is monotone in s for c >= 0: the max of x is x of the max.
+            float xa = fmaf(ma, c, -m_a), xb = fmaf(mb, c, -m_b);
+            xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 1));
+            xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 1));
+            xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 2));
+            xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 2));
+            if (xa > kRescaleLog2) {
+              f_a = ex2_approx(-xa);
+              m_a += xa;
+              rescale = true;
+            }
+            if (xb > kRescaleLog2) {
+              f_b = ex2_approx(-xb);
+              m_b += xb;
+              rescale = true;
+            }
+            if (__any_sync(0xffffffffu, rescale)) {
+              // Redo P against the raised maxima.
+              tmem_wait_st();
+              rs_a = 0ull;
+              rs_b = 0ull;
+#pragma unroll
+              for (int half = 0; half < 2; ++half) {
+                uint32_t pk[16];
+                p_rows<kEmu, false>(s + 32 * half, c, -m_a, -m_b, rs_a, rs_b, pk);
+                tmem_st_16x128b_x8(tS + 32 * half, pk);
+              }
+              rescale_o();
+            }
+          }
         } else {
-          mx = row_max128(s) * c;  // c >= 0: the max of s*c is c times the max
+          float mx_a, mx_b;
+          if (masked) {
+            // Scale first, then mask, so masked keys are exactly -inf for any scale.
+            const int va = lim_a - kbase - 2 * t0, vb = lim_b - kbase - 2 * t0;
+            mx_a = -INFINITY;
+            mx_b = -INFINITY;
+#pragma unroll
+            for (int g = 0; g < 16; ++g) {
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const float xa = 8 * g + e < va ? s[4 * g + e] * c : -INFINITY;
+                const float xb = 8 * g + e < vb ? s[4 * g + 2 + e] * c : -INFINITY;
+                s[4 * g + e] = xa;
+                s[4 * g + 2 + e] = xb;
+                mx_a = fmaxf(mx_a, xa);
+                mx_b = fmaxf(mx_b, xb);
+              }
+            }
+          } else {
+            // Four independent chains per row over the 16 repeats.
+            float a[4], b[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              a[u] = fmaxf(s[4 * u], s[4 * u + 1]);
+              b[u] = fmaxf(s[4 * u + 2], s[4 * u + 3]);
+            }
+#pragma unroll
+            for (int g = 4; g < 16; ++g) {
+              a[g & 3] = fmax3(a[g & 3], s[4 * g], s[4 * g + 1]);
+              b[g & 3] = fmax3(b[g & 3], s[4 * g + 2], s[4 * g + 3]);
+            }
+            mx_a = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])) * c;
+            mx_b = fmaxf(fmaxf(b[0], b[1]), fmaxf(b[2], b[3])) * c;
+          }
+          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+          tr(kEvSmMaxDone, warp >> 2, tt);
+          // Running-max update with lazy rescaling (per row; the four
+          // threads of a row hold the same values, so they decide alike).
+          if (m_a == -INFINITY) {
+            m_a = mx_a;  // no probability mass accumulated yet for this row
+          } else if (mx_a > m_a + kRescaleLog2) {
+            f_a = ex2_approx(m_a - mx_a);
+            m_a = mx_a;
+            rescale = true;
+          }
+          if (m_b == -INFINITY) {
+            m_b = mx_b;
+          } else if (mx_b > m_b + kRescaleLog2) {
+            f_b = ex2_approx(m_b - mx_b);
+            m_b = mx_b;
+            rescale = true;
+          }
+          const bool rescale_w = __any_sync(0xffffffffu, rescale);
+          all_finite = __all_sync(0xffffffffu, m_a != -INFINITY && m_b != -INFINITY);
+          const float nm_a = (m_a == -INFINITY) ? 0.0f : -m_a;
+          const float nm_b = (m_b == -INFINITY) ? 0.0f : -m_b;
+          const float sc = masked ? 1.0f : c;  // masked scores are pre-scaled
+          // P for keys 0-63 (repeats g = 0..7), then 64-127 (g = 8..15).
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t pk[16];
+            if (masked)
+              p_rows<kEmu, true>(s + 32 * half, sc, nm_a, nm_b, rs_a, rs_b, pk);
+            else
+              p_rows<kEmu, false>(s + 32 * half, sc, nm_a, nm_b, rs_a, rs_b, pk);
+            tmem_st_16x128b_x8(tS + 32 * half, pk);
+          }
+          ready = mbar_try_wait(smem_u32(&s_ready[nb]), static_cast<uint32_t>((tt + 1) / kSBufs) & 1u);
+          ready_all = __all_sync(0xffffffffu, ready);
+          if (rescale_w && j > 0) rescale_o();
         }
-        tr(kEvSmMaxDone, pipe, tt);
-        float f = 1.0f;
-        bool rescale = false;
-        if (m == -INFINITY) {
-          m = mx;  // no probability mass accumulated yet for this row
-        } else if (mx > m + kRescaleLog2) {
-          f = ex2_approx(m - mx);
-          m = mx;
-          rescale = true;
+        tr(kEvSmPComputed, warp >> 2, tt);
+        // S(tt+1) (the next item's first tile after an item's last), if it is
+        // already computed: its load starts once P(tt) is published.
+        have_s = ready_all && tt + 1 < g_total && ok;
+        if (ok) {
+          // Publish P(tt) (and any O rescale) before S(tt+1)'s load is
+          // issued: the store wait and fence would otherwise also wait for
+          // that load (measured 2 % slower).
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          mbar_arrive_warp(&p_ready[sb]);
+          tr(kEvSmPublished, warp >> 2, tt);
         }
-        const float nm = (m == -INFINITY) ? 0.0f : -m;
-        uint64_t ra = 0ull, rb = 0ull;
-        if (masked)
-          p_tile<kEmu, true>(s, c, nm, va, tS, ra, rb);
-        else
-          p_tile<kEmu, false>(s, c, nm, 128, tS, ra, rb);
-        // O rows of this pipe follow a raised max (the pipe's first tile of
-        // the item needs none: its PV overwrites O).
-        if (!first && __any_sync(0xffffffffu, rescale)) rescale_o(f);
-        tr(kEvSmPComputed, pipe, tt);
-        // Publish P(tt) (and any O rescale) to the MMA issuer.
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        mbar_arrive_warp(&p_ready[pipe]);
-        tr(kEvSmPublished, pipe, tt);
-        {
-          float e0, e1;
-          f2_unpack(f2_add(ra, rb), e0, e1);
-          l = fmaf(l, f, e0 + e1);
+        if (have_s) {
+          tc_fence_after();
+          load_s(tmem_base + lane_addr + static_cast<uint32_t>(nb * 128));
         }
+        l2_a = f2_fma(l2_a, f2_pack(f_a, f_a), rs_a);
+        l2_b = f2_fma(l2_b, f2_pack(f_b, f_b), rs_b);
+        if (!ok) break;
       }
       if (!ok) break;
-      // This pipe's (m, l) for the item, handed to the epilogue once it has
-      // finished the previous item (li - 1) and read its values.
+      // Row sums over the four threads of each row, handed to the epilogue
+      // once it has finished the previous item (li - 1) and read its sums.
+      float l_a, l_b;
+      {
+        float e0, e1;
+        f2_unpack(l2_a, e0, e1);
+        l_a = e0 + e1;
+        f2_unpack(l2_b, e0, e1);
+        l_b = e0 + e1;
+      }
+      l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+      l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+      l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+      l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
       ok = warp_wait(o_empty, (static_cast<uint32_t>(li) & 1u) ^ 1u, kSiteOEmpty);
       if (!ok) break;
-      stat[pipe * 128 + row] = make_float2(m, l);
+      if (t0 == 0) {
+        lsum[qb * 128 + ra] = l_a;
+        lsum[qb * 128 + rb] = l_b;
+      }
       __syncwarp();
       mbar_arrive_warp(&l_ready[qb]);
-      tr(kEvSmItemEnd, pipe, li);
+      tr(kEvSmItemEnd, warp >> 2, li);
       t += it.n;
       ++li;
+    }
+    if (have_s) {
+      // Abandoned prefetch (only after an abort): let the load land.
+      tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
     }
   } else {
     setmaxnreg_dec<kEpiRegs>();
@@ -724,8 +886,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t quad = warp & 3u;
     const int row = static_cast<int>(quad * 32 + lane);
     const uint32_t lane_addr = (quad * 32u) << 16;
-    const uint32_t tO0 = tmem_base + lane_addr + C::kColO;
-    const uint32_t tO1 = tO0 + D;
     Tracer<kTrace> tr(p, 4, trace_cta && quad == 0 && lane == 0);
     int li = 0;
 #pragma unroll 1
@@ -742,50 +902,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           warp_wait(&l_ready[qb], qpar, kSiteLReady);
       if (!got) abort_flag[0] = 1;
       tc_fence_after();
-      const bool have_o = got && it.n > 0;  // warp-uniform
-      // Merge weights: f_p = 2^(m_p - m) / l for pipes with mass, else 0 (a
-      // pipe without mass for this row may hold a stale accumulator).
-      float f0 = 0.0f, f1 = 0.0f;
-      if (have_o) {
-        const float2 s0 = stat[row];
-        const float2 s1 = stat[128 + row];
-        const float mm = fmaxf(s0.x, s1.x);
-        const float w0 = s0.y > 0.0f ? ex2_approx(s0.x - mm) : 0.0f;
-        const float w1 = s1.y > 0.0f ? ex2_approx(s1.x - mm) : 0.0f;
-        const float l = s0.y * w0 + s1.y * w1;
-        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-        f0 = w0 * inv;
-        f1 = w1 * inv;
-      }
+      const uint32_t tO = tmem_base + lane_addr + C::kColO;
+      const float l = lsum[qb * 128 + row];
+      const bool have_o = got && it.n > 0;
+      const float inv = (have_o && l > 0.0f) ? 1.0f / l : 0.0f;
       uint8_t* obuf = q_buf + qb * C::kTileBytes;
       const uint32_t obase = smem_u32(obuf);
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 16) {
-        uint32_t o[32];  // [0,16) pipe 0, [16,32) pipe 1
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
         if (have_o) {
-          tmem_ld16(tO0 + c0, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
-          tmem_ld16(tO1 + c0, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+          tmem_ld32(tO + c0, o);
           tmem_wait_ld(o);
         } else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = 0u;
         }
-        uint32_t w[8];
+        uint32_t w[16];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          float v[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float a = __uint_as_float(o[2 * e + h]);
-            const float b = __uint_as_float(o[16 + 2 * e + h]);
-            v[h] = (f0 != 0.0f ? a * f0 : 0.0f) + (f1 != 0.0f ? b * f1 : 0.0f);
-          }
-          w[e] = pack_bf16x2(v[0], v[1]);
-        }
+        for (int e = 0; e < 16; ++e)
+          w[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
         const int box = c0 >> 6;
         const int chunk0 = (c0 & 63) >> 3;  // 16-byte chunk index inside the 128-byte row
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < 4; ++u) {
           const int ch = (chunk0 + u) ^ (row & 7);
           st_shared_v4(obase + box * C::kBoxBytes + row * 128 + ch * 16, w[4 * u], w[4 * u + 1],
                        w[4 * u + 2], w[4 * u + 3]);

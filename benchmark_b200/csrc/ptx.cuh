@@ -662,6 +662,14 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// 2^e for an integer-valued e (or -inf), built in the exponent field: exact,
+// 0 below 2^-126 (and for -inf), +inf above 2^127.
+__device__ __forceinline__ float exp2i(float e) {
+  if (e < -126.0f) return 0.0f;
+  if (e > 127.0f) return __int_as_float(0x7f800000);
+  return __int_as_float((static_cast<int>(e) + 127) << 23);
+}
+
 // Packed fp32 pairs (sm_100 f32x2 arithmetic): lo in bits 0-31.
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   uint64_t r;

@@ -109,6 +109,24 @@ def test_large_scores_exercise_rescale():
     gate(to_host_f32(o), ref, "rescale")
 
 
+@pytest.mark.parametrize("slope,causal", [(0.05, False), (0.05, True), (0.004, False),
+                                          (-0.05, False)])
+def test_reference_max_raises_every_tile(slope, causal):
+    """Scores that climb along the keys by about 100 log2 units per 128-key
+    tile (slope 0.05; 0.004 climbs by about 8 per tile, -0.05 falls) force the
+    shared reference maximum up on (nearly) every tile, alternately in each
+    softmax pipe, so the P conversion and O rescale paths run on most tiles."""
+    B, H, S, D = 1, 2, 4096, 128
+    q = torch.ones((B, H, 256, D), dtype=torch.bfloat16, device="cuda")
+    ramp = (torch.arange(S, device="cuda", dtype=torch.float32) * slope).view(1, 1, S, 1)
+    k = (torch.ones((B, H, S, D), device="cuda") * ramp).to(torch.bfloat16).contiguous()
+    _, _, v = normal_inputs(B, H, H, 1, S, D, seed=13)
+    o = ops.attention_fwd(q, k, v, causal=causal)
+    ops.check()
+    ref = oracle.attention(to_host_bits(q), to_host_bits(k), to_host_bits(v), causal=causal)
+    gate(to_host_f32(o), ref, f"raises slope {slope} causal {causal}")
+
+
 def test_baseline_config2_full_size():
     """BASELINE config 2 (B4 H32 N4096 d128): full tensor vs the scalar
     kernel, oracle rows on a sample of heads, deterministic across runs."""
