@@ -18,7 +18,7 @@
 //               ahead of the V ring's slower turnover)
 //   warp  15    idle; it completes warpgroup 3, so that each warpgroup can
 //               move its register budget with setmaxnreg (softmax 184,
-//               epilogue 56, producers/issuer 88 registers per thread)
+//               epilogue 64, producers/issuer 80 registers per thread)
 //
 // TMEM (512 columns): three S buffers [0,128) [128,256) [256,384) rotate over
 // the global tile sequence; O at [384, 384+D).  P (bf16 pairs) overwrites the
@@ -54,6 +54,13 @@
 // of its own tile, before the next tile's scores are loaded: a TMEM store
 // wait or fence behind an outstanding TMEM load waits for that load too.
 //
+// Short problems (too few Q tiles to fill the SMs) split each Q tile's K/V
+// tiles among nsplit work units.  A unit's epilogue writes its unnormalised
+// O rows and per-row (m, l) to a workspace in global memory, fences, and
+// counts itself in the Q tile's counter; the unit that completes the count
+// merges all units (O = sum_u O_u 2^(m_u - m) / sum_u l_u 2^(m_u - m)),
+// stores O and resets the counter.  No second launch is needed.
+//
 // Every wait is bounded (ptx.cuh).  A timeout sets the device status word;
 // the epilogue warps, which meet at a named barrier, agree on aborting
 // through a shared flag written before the barrier, so no barrier is ever
@@ -77,8 +84,8 @@ constexpr int kThreads = 512;  // warp 15 only completes warpgroup 3
 // the pool the block launches with (512 threads x 128).
 constexpr int kLaunchRegs = 65536 / kThreads;
 constexpr int kSoftmaxRegs = 184;
-constexpr int kEpiRegs = 56;
-constexpr int kCtlRegs = 88;
+constexpr int kEpiRegs = 64;
+constexpr int kCtlRegs = 80;
 static_assert(8 * 32 * kSoftmaxRegs + 4 * 32 * kEpiRegs + 4 * 32 * kCtlRegs ==
                   kThreads * kLaunchRegs,
               "register split must use exactly the launch pool");
@@ -95,11 +102,19 @@ struct Params {
   int B, Hq, Hkv, Sq, Skv;
   int group;     // Hq / Hkv
   int n_qtiles;  // ceil(Sq / 128)
-  int n_items;   // B * Hq * n_qtiles
+  int n_items;   // work units: B * Hq * n_qtiles * nsplit
   int causal;      // bottom-right aligned
   int causal_off;  // Skv - Sq
   int cgroup;      // causal: Q planes per ordering group (their K/V fit in L2 together)
   int kv_evict_first;  // L2 policy of the K/V loads: 1 evict_first, 0 evict_last
+  // Split K/V ranges (short sequences): each Q tile's K/V tiles are divided
+  // among nsplit work units; a unit writes its unnormalised O rows and (m, l)
+  // to ws_o / ws_ml, and the last unit of a Q tile to finish (ws_cnt) merges
+  // them and stores O.  nsplit = 1: no split, the ws_* are unused.
+  int nsplit;
+  float* ws_o;          // [units][128][D]
+  float2* ws_ml;        // [units][128] (m in log2 units, l)
+  unsigned* ws_cnt;     // [Q tiles] arrivals; the merging unit resets it to 0
   float scale_log2;  // softmax_scale * log2(e)
   // Clock trace (kTrace instantiations only): per-role record regions of
   // trace_cap records (2 x u64: (event << 32 | tile << 24 | iter), clock64)
@@ -152,8 +167,10 @@ struct Cfg {
   static constexpr int kQOff = 0;                       // Q0, Q1 (also O staging)
   static constexpr int kKOff = 2 * kTileBytes;
   static constexpr int kVOff = kKOff + kKStages * kTileBytes;
-  static constexpr int kLOff = kVOff + kVStages * kTileBytes;  // row sums [2 items][128]
-  static constexpr int kFlagOff = kLOff + 2 * 128 * 4;        // abort flag (epilogue)
+  // per-row (m, l) of the item the epilogue works on: one slot suffices, the
+  // softmax writes item li's values only after the epilogue released li-1
+  static constexpr int kLOff = kVOff + kVStages * kTileBytes;
+  static constexpr int kFlagOff = kLOff + 128 * 8;  // abort flag and merge flag (epilogue)
   static constexpr int kBarOff = kFlagOff + 16;
   // q_full[2] q_empty[2] k_full[K] k_empty[K] v_full[V] v_empty[V]
   // s_ready[3] p_ready[3] pv_done o_full o_empty l_ready[2] drain done
@@ -192,15 +209,20 @@ struct Item {
   int zq;    // (b * Hq + hq): plane of Q / O
   int zkv;   // (b * Hkv + hkv): plane of K / V
   int row0;  // first query row
+  int j0;    // first K/V tile of this unit (split K/V ranges; else 0)
   int n;     // K/V tiles to visit
   int min_lim;
+  int tile;  // Q tile index (unit / nsplit): the merge counter of split units
 };
 
 // Work item k.  Non-causal: items of one head are adjacent, so the CTAs
 // running at one time share a few heads' K/V in L2.  Causal: planes are taken
 // in groups of p.cgroup (sized on the host so that a group's K/V fit in L2
 // together); inside a group the heaviest Q tiles (last rows) come first.
-__device__ __forceinline__ Item decode_item(const Params& p, int k) {
+__device__ __forceinline__ Item decode_item(const Params& p, int unit) {
+  // A Q tile's split units are adjacent, so they run at the same time.
+  const int k = unit / p.nsplit;
+  const int split = unit - k * p.nsplit;
   const int bhs = p.B * p.Hq;
   int bh, qt;
   if (p.causal) {
@@ -220,7 +242,11 @@ __device__ __forceinline__ Item decode_item(const Params& p, int k) {
   it.zq = bh;
   it.zkv = b * p.Hkv + hq / p.group;
   it.row0 = qt * kBM;
-  tile_extent(p, it.row0, &it.n, &it.min_lim);
+  int n_all;
+  tile_extent(p, it.row0, &n_all, &it.min_lim);
+  it.j0 = n_all * split / p.nsplit;
+  it.n = n_all * (split + 1) / p.nsplit - it.j0;
+  it.tile = k;
   return it;
 }
 
@@ -298,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* q_buf = smem + C::kQOff;
   uint8_t* k_buf = smem + C::kKOff;
   uint8_t* v_buf = smem + C::kVOff;
-  float* lsum = reinterpret_cast<float*>(smem + C::kLOff);
+  float2* stat = reinterpret_cast<float2*>(smem + C::kLOff);  // [row] = (m, l)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kFlagOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* q_full = bars;
@@ -347,6 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(done, 1);
     mbar_arrive(done);
     abort_flag[0] = 0;
+    abort_flag[1] = 0;
     fence_mbar_init();
   }
   if (warp == kTmaWarp) {
@@ -407,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               mbar_arrive_expect_tx(&k_full[ks], C::kTileBytes);
               for (int h = 0; h < C::kBoxes; ++h)
                 tma_load_3d(k_buf + ks * C::kTileBytes + h * C::kBoxBytes, &k_map, &k_full[ks],
-                            h * 64, j * kBN, it.zkv, pol_kv);
+                            h * 64, (it.j0 + j) * kBN, it.zkv, pol_kv);
             } else {
               const int vs = t % C::kVStages;
               ok = mbar_wait(&v_empty[vs], (static_cast<uint32_t>(t / C::kVStages) & 1u) ^ 1u,
@@ -417,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               mbar_arrive_expect_tx(&v_full[vs], C::kTileBytes);
               for (int h = 0; h < C::kBoxes; ++h)
                 tma_load_3d(v_buf + vs * C::kTileBytes + h * C::kBoxBytes, &v_map, &v_full[vs],
-                            h * 64, j * kBN, it.zkv, pol_kv);
+                            h * 64, (it.j0 + j) * kBN, it.zkv, pol_kv);
             }
             issued = t + 1;
           }
@@ -655,7 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         have_s = false;
         tr(kEvSmLdDone, warp >> 2, tt);
         float* s = reinterpret_cast<float*>(sr);
-        const int kbase = j * kBN;
+        const int kbase = (it.j0 + j) * kBN;
         const bool masked = kbase + kBN > it.min_lim;  // uniform across the tile
         float f_a = 1.0f, f_b = 1.0f;
         bool rescale = false;    // this thread's rows
@@ -866,8 +893,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = warp_wait(o_empty, (static_cast<uint32_t>(li) & 1u) ^ 1u, kSiteOEmpty);
       if (!ok) break;
       if (t0 == 0) {
-        lsum[qb * 128 + ra] = l_a;
-        lsum[qb * 128 + rb] = l_b;
+        stat[ra] = make_float2(m_a, l_a);
+        stat[rb] = make_float2(m_b, l_b);
       }
       __syncwarp();
       mbar_arrive_warp(&l_ready[qb]);
@@ -903,44 +930,171 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!got) abort_flag[0] = 1;
       tc_fence_after();
       const uint32_t tO = tmem_base + lane_addr + C::kColO;
-      const float l = lsum[qb * 128 + row];
+      const float2 ml = stat[row];  // (m, l) of this row
       const bool have_o = got && it.n > 0;
-      const float inv = (have_o && l > 0.0f) ? 1.0f / l : 0.0f;
       uint8_t* obuf = q_buf + qb * C::kTileBytes;
       const uint32_t obase = smem_u32(obuf);
-#pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t o[32];
-        if (have_o) {
-          tmem_ld32(tO + c0, o);
-          tmem_wait_ld(o);
-        } else {
+      // Pack 16 fp32 values of this row (columns c0..c0+15) to bf16 and
+      // stage them in the 128-byte-swizzled O tile.
+      auto stage16 = [&](int c0, const float* v) {
+        uint32_t w[8];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = 0u;
-        }
-        uint32_t w[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          w[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+        for (int e = 0; e < 8; ++e) w[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
         const int box = c0 >> 6;
         const int chunk0 = (c0 & 63) >> 3;  // 16-byte chunk index inside the 128-byte row
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 2; ++u) {
           const int ch = (chunk0 + u) ^ (row & 7);
           st_shared_v4(obase + box * C::kBoxBytes + row * 128 + ch * 16, w[4 * u], w[4 * u + 1],
                        w[4 * u + 2], w[4 * u + 3]);
         }
+      };
+      // 8 values (columns c0..c0+7, c0 % 8 == 0): one 16-byte chunk.
+      auto stage8 = [&](int c0, const float* v) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+        const int ch = ((c0 & 63) >> 3) ^ (row & 7);
+        st_shared_v4(obase + (c0 >> 6) * C::kBoxBytes + row * 128 + ch * 16, w[0], w[1], w[2],
+                     w[3]);
+      };
+      bool store = true;  // this unit stores the O tile
+      if (p.nsplit == 1) {
+        const float inv = (have_o && ml.y > 0.0f) ? 1.0f / ml.y : 0.0f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          if (have_o) {
+            tmem_ld32(tO + c0, o);
+            tmem_wait_ld(o);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0u;
+          }
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * inv);
+          stage16(c0, reinterpret_cast<const float*>(&o[0]));
+          stage16(c0 + 16, reinterpret_cast<const float*>(&o[16]));
+        }
+        tc_fence_before();
+        mbar_arrive(o_empty);
+      } else {
+        // Split unit: this unit's unnormalised O rows and (m, l) go to the
+        // workspace; the Q tile's last unit to arrive merges all of them.
+        float* my_o = p.ws_o + (static_cast<size_t>(k) * 128 + row) * D;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          if (have_o) {
+            tmem_ld32(tO + c0, o);
+            tmem_wait_ld(o);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0u;
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            reinterpret_cast<uint4*>(my_o + c0)[e] =
+                make_uint4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+        }
+        p.ws_ml[static_cast<size_t>(k) * 128 + row] =
+            have_o ? ml : make_float2(-INFINITY, 0.0f);
+        __threadfence();
+        named_bar_sync(kBarEpilogue, 128);  // every row of this unit is written
+        if (quad == 0 && lane == 0) {
+          int last = 0;
+          if (abort_flag[0] == 0) {
+            const unsigned prev = atomicAdd(&p.ws_cnt[it.tile], 1u);
+            last = prev == static_cast<unsigned>(p.nsplit - 1);
+            if (last) p.ws_cnt[it.tile] = 0u;  // every unit has arrived: reset for the next call
+          }
+          abort_flag[1] = last;
+        }
+        named_bar_sync(kBarEpilogue, 128);
+        store = abort_flag[1] != 0;
+        if (store) {
+          // Merge: this unit's rows come from TMEM (O is released only
+          // afterwards), the other units' from the workspace (L2).
+          __threadfence();
+          const int u0 = it.tile * p.nsplit;
+          float mmax = -INFINITY;
+          for (int sp = 0; sp < p.nsplit; ++sp)
+            mmax = fmaxf(mmax, __ldcg(&p.ws_ml[static_cast<size_t>(u0 + sp) * 128 + row]).x);
+          float lsum = 0.0f;
+          for (int sp = 0; sp < p.nsplit; ++sp) {
+            const float2 v = __ldcg(&p.ws_ml[static_cast<size_t>(u0 + sp) * 128 + row]);
+            if (v.y > 0.0f) lsum += v.y * ex2_approx(v.x - mmax);
+          }
+          const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+          const float w_own = (have_o && ml.y > 0.0f) ? ex2_approx(ml.x - mmax) * inv : 0.0f;
+#pragma unroll 1
+          for (int c0 = 0; c0 < D; c0 += 8) {
+            // Units are added in unit order (this unit's rows from TMEM at
+            // its own place), so the result does not depend on which unit
+            // arrived last.
+            uint32_t own[8];
+            if (have_o) {
+              tmem_ld8(tO + c0, own);
+              tmem_wait_ld();
+              reg_written_here8(own);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) own[e] = 0u;
+            }
+            float acc[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+#pragma unroll 1
+            for (int sp = 0; sp < p.nsplit; sp += 2) {
+              float4 x[2][2];
+              float w[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int uu = u0 + sp + h;
+                const bool use = sp + h < p.nsplit && uu != k;
+                const float2 v = use ? __ldcg(&p.ws_ml[static_cast<size_t>(uu) * 128 + row])
+                                     : make_float2(-INFINITY, 0.0f);
+                w[h] = uu == k ? w_own : (v.y > 0.0f ? ex2_approx(v.x - mmax) * inv : 0.0f);
+                const float4* src = reinterpret_cast<const float4*>(
+                    p.ws_o + (static_cast<size_t>(use ? uu : k) * 128 + row) * D + c0);
+                if (uu == k) {
+                  x[h][0] = make_float4(__uint_as_float(own[0]), __uint_as_float(own[1]),
+                                        __uint_as_float(own[2]), __uint_as_float(own[3]));
+                  x[h][1] = make_float4(__uint_as_float(own[4]), __uint_as_float(own[5]),
+                                        __uint_as_float(own[6]), __uint_as_float(own[7]));
+                } else {
+                  x[h][0] = __ldcg(src);
+                  x[h][1] = __ldcg(src + 1);
+                }
+              }
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                if (w[h] == 0.0f) continue;  // no mass: its rows may hold anything
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  acc[4 * e + 0] = fmaf(x[h][e].x, w[h], acc[4 * e + 0]);
+                  acc[4 * e + 1] = fmaf(x[h][e].y, w[h], acc[4 * e + 1]);
+                  acc[4 * e + 2] = fmaf(x[h][e].z, w[h], acc[4 * e + 2]);
+                  acc[4 * e + 3] = fmaf(x[h][e].w, w[h], acc[4 * e + 3]);
+                }
+              }
+            }
+            stage8(c0, acc);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(o_empty);
       }
-      tc_fence_before();
-      mbar_arrive(o_empty);
       fence_proxy_async_smem();
       named_bar_sync(kBarEpilogue, 128);
       if (abort_flag[0] != 0) break;
       if (quad == 0 && lane == 0) {
-        for (int b = 0; b < C::kBoxes; ++b)
-          tma_store_3d(&o_map, obuf + b * C::kBoxBytes, b * 64, it.row0, it.zq);
-        bulk_commit_group();
-        bulk_wait_group_read<0>();
+        if (store) {
+          for (int b = 0; b < C::kBoxes; ++b)
+            tma_store_3d(&o_map, obuf + b * C::kBoxBytes, b * 64, it.row0, it.zq);
+          bulk_commit_group();
+          bulk_wait_group_read<0>();
+        }
         mbar_arrive(&q_empty[qb]);
       }
       tr(kEvEpiEnd, qb, li - 1);

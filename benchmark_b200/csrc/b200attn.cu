@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <string>
@@ -250,6 +251,79 @@ struct TraceArgs {
   int cta = -1;
 };
 
+// Split K/V ranges for short problems: when the Q tiles cannot fill half the
+// SMs and their K/V ranges are long, each Q tile's K/V tiles are divided among
+// up to 8 work units (at least 16 K/V tiles each) so that the grid fills the
+// GPU; the units' partial results meet in a workspace and the last unit of
+// each Q tile merges them.  Measured on B200 (one head, d=128): N=8192 588 ->
+// 691 TFLOP/s (causal 295 -> 375) with 2 units per Q tile; with 32 K/V tiles
+// per Q tile (2 heads, N=4096) the merge cost more than the split saved
+// (519 -> 466), and with 8 (config 1) the units' fixed costs alone did.
+int split_count(long long qtiles, int kv_tiles, int sms) {
+  if (qtiles * 2 > sms || kv_tiles < 48) return 1;
+  const long long n = std::min<long long>({sms / qtiles, kv_tiles / 16, 8});
+  return static_cast<int>(std::max<long long>(n, 1));
+}
+
+// Workspace of the split units, one per (device, stream) so that calls on
+// different streams never share it; grown on demand, never shrunk.
+struct SplitWorkspace {
+  float* o = nullptr;       // [units][128][128] fp32 (d=64 uses the first 64 columns' worth)
+  float2* ml = nullptr;     // [units][128]
+  unsigned* cnt = nullptr;  // [Q tiles], zero between calls
+  size_t units = 0, tiles = 0;
+};
+
+std::mutex& split_mutex() {
+  static std::mutex m;
+  return m;
+}
+
+std::map<std::pair<int, cudaStream_t>, SplitWorkspace>& split_workspaces() {
+  static std::map<std::pair<int, cudaStream_t>, SplitWorkspace> w;
+  return w;
+}
+
+b200_status split_workspace(cudaStream_t stream, size_t units, size_t tiles, SplitWorkspace* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(split_mutex());
+  SplitWorkspace& w = split_workspaces()[{dev, stream}];
+  if (w.units < units || w.tiles < tiles) {
+    // Earlier calls on this stream may still use the old buffers.
+    if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return cuda_fail(e, "workspace sync");
+    cudaFree(w.o);
+    cudaFree(w.ml);
+    cudaFree(w.cnt);
+    w = SplitWorkspace{};
+    const size_t nu = std::max(units, static_cast<size_t>(256));
+    const size_t nt = std::max(tiles, static_cast<size_t>(128));
+    if ((e = cudaMalloc(&w.o, nu * 128 * 128 * sizeof(float))) != cudaSuccess ||
+        (e = cudaMalloc(&w.ml, nu * 128 * sizeof(float2))) != cudaSuccess ||
+        (e = cudaMalloc(&w.cnt, nt * sizeof(unsigned))) != cudaSuccess ||
+        (e = cudaMemset(w.cnt, 0, nt * sizeof(unsigned))) != cudaSuccess) {
+      cudaFree(w.o);
+      cudaFree(w.ml);
+      cudaFree(w.cnt);
+      w = SplitWorkspace{};
+      return cuda_fail(e, "attention split workspace");
+    }
+    w.units = nu;
+    w.tiles = nt;
+  }
+  *out = w;
+  return B200_OK;
+}
+
+// After a failed call the merge counters may hold partial counts: zero them.
+void reset_split_counters(int dev) {
+  std::lock_guard<std::mutex> lock(split_mutex());
+  for (auto& kv : split_workspaces())
+    if (kv.first.first == dev && kv.second.cnt)
+      cudaMemset(kv.second.cnt, 0, kv.second.tiles * sizeof(unsigned));
+}
+
 template <int D, int EMU, bool TRACE = false>
 b200_status launch_attention(const void* q, const void* k, const void* v, void* o,
                              const AttnShape& s, cudaStream_t stream,
@@ -289,9 +363,21 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   p.Skv = s.Skv;
   p.group = s.Hq / s.Hkv;
   p.n_qtiles = (s.Sq + b200::attn::kBM - 1) / b200::attn::kBM;
-  const long long items = static_cast<long long>(pq) * p.n_qtiles;
+  const long long qtiles = static_cast<long long>(pq) * p.n_qtiles;
+  const int kv_tiles = (s.Skv + b200::attn::kBN - 1) / b200::attn::kBN;
+  p.nsplit = split_count(qtiles, kv_tiles, sm_count());
+  const long long items = qtiles * p.nsplit;
   if (items > 0x3fffffffll) return fail(B200_EUNSUPPORTED, "attention: too many work items");
   p.n_items = static_cast<int>(items);
+  if (p.nsplit > 1) {
+    SplitWorkspace w;
+    if ((st = split_workspace(stream, static_cast<size_t>(items), static_cast<size_t>(qtiles),
+                              &w)) != B200_OK)
+      return st;
+    p.ws_o = w.o;
+    p.ws_ml = w.ml;
+    p.ws_cnt = w.cnt;
+  }
   p.causal = s.causal;
   p.causal_off = s.Skv - s.Sq;
   // Causal items are ordered in groups of planes whose K/V (shared by the
@@ -461,6 +547,8 @@ b200_status b200_check(b200_stream_t stream) {
     const uint32_t zero = 0;
     e = cudaMemcpyToSymbol(b200::g_status, &zero, sizeof(zero));
     if (e != cudaSuccess) return cuda_fail(e, "clear status word");
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) reset_split_counters(dev);
     const uint32_t site = (status >> 8) & 0xffu;
     if (site == b200::attn::kSiteSmemLayout)
       return fail(B200_ECUDA, "attention kernel: dynamic shared memory starts too far past a "

@@ -588,6 +588,12 @@ __device__ __forceinline__ void tmem_st_16x128b_x8(uint32_t taddr, const uint32_
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : B200_R8(r, 0)
+               : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
@@ -643,6 +649,10 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
 // any use of them above that wait.
 __device__ __forceinline__ void reg_written_here(uint32_t (&r)[32]) {
   asm volatile("" : B200_RW8(r, 0), B200_RW8(r, 8), B200_RW8(r, 16), B200_RW8(r, 24));
+}
+
+__device__ __forceinline__ void reg_written_here8(uint32_t (&r)[8]) {
+  asm volatile("" : B200_RW8(r, 0));
 }
 
 __device__ __forceinline__ void reg_written_here16(uint32_t (&r)[16]) {

@@ -8,7 +8,14 @@
  *
  * Conventions
  *   - All tensor pointers are device pointers owned by the caller, 16-byte
- *     aligned, contiguous.  Nothing here allocates on the hot path.
+ *     aligned, contiguous.
+ *   - attention_fwd splits the K/V range of short problems (too few 128-row
+ *     Q tiles to fill the GPU, K/V ranges of 48 or more 128-key tiles) among
+ *     several CTAs that merge through a workspace.  The workspace belongs to
+ *     the library, one per (device, stream); the first such call on a
+ *     (device, stream) allocates it (cudaMalloc, which synchronises the
+ *     device) and later calls reuse it, growing it when a larger problem
+ *     needs more.  Nothing else allocates.
  *   - bf16 tensors are passed as raw 16-bit words (uint16_t storage).
  *   - Calls are asynchronous on `stream` (NULL = legacy default stream) and
  *     use the calling thread's current CUDA device.

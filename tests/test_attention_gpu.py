@@ -85,6 +85,47 @@ def test_medium_vs_torch_fp32_and_scalar(D, causal):
     gate(to_host_f32(s), ref, "scalar vs torch fp32")
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,Sq,Skv,D,causal", [
+    (1, 1, 1, 128, 8192, 128, False),    # one Q tile, 64 K/V tiles: 4 split units
+    (1, 2, 1, 300, 6500, 64, False),     # ragged, GQA, d=64: 3 units
+    (1, 4, 2, 256, 7000, 128, True),     # causal: 3 units of different lengths
+    (1, 1, 1, 6500, 6200, 128, True),    # Sq > Skv: units with no valid key
+    (1, 1, 1, 6144, 6144, 128, False),   # 48 Q tiles x 3 units
+    (1, 1, 1, 100, 7000, 128, False),    # one ragged Q tile, 3 units of 18 or 19 tiles
+])
+def test_split_kv_units_vs_oracle(B, Hq, Hkv, Sq, Skv, D, causal):
+    """Short problems split each Q tile's K/V range among several CTAs that
+    merge through a workspace; three calls in a row (the merge counters must
+    return to zero after each) give identical bytes and pass the gate."""
+    q, k, v = normal_inputs(B, Hq, Hkv, Sq, Skv, D, seed=21)
+    outs = []
+    for _ in range(3):
+        o = ops.attention_fwd(q, k, v, causal=causal)
+        ops.check()
+        outs.append(to_host_bits(o))
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+    ref = oracle.attention(to_host_bits(q), to_host_bits(k), to_host_bits(v), causal=causal)
+    gate(oracle.bf16_to_f32(outs[0]), ref, f"split B{B} Hq{Hq} Sq{Sq} Skv{Skv} D{D} c{int(causal)}")
+
+
+def test_split_kv_on_two_streams():
+    """Calls on different streams use separate workspaces."""
+    q, k, v = normal_inputs(1, 2, 2, 256, 8192, 128, seed=22)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    o1 = torch.empty_like(q)
+    o2 = torch.empty_like(q)
+    torch.cuda.synchronize()
+    for _ in range(4):
+        ops.attention_fwd(q, k, v, out=o1, stream=s1)
+        ops.attention_fwd(q, k, v, out=o2, stream=s2)
+    torch.cuda.synchronize()
+    ops.check(s1)
+    ops.check(s2)
+    assert torch.equal(o1, o2)
+    ref = oracle.attention(to_host_bits(q), to_host_bits(k), to_host_bits(v))
+    gate(to_host_f32(o1), ref, "two streams")
+
+
 def test_custom_scale_and_zero_scale():
     q, k, v = normal_inputs(1, 2, 2, 300, 400, 128, seed=3)
     for scale, causal in ((0.3, False), (0.0, True), (0.02, True)):
