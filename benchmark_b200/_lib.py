@@ -37,6 +37,7 @@ _PROTOTYPES = {
     "attention_fwd_trace": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _i, _i,
                             _vp],
     "attention_fwd_scalar": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp],
+    "attention_fwd_noalloc": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _i, _vp],
     "b200_fill_normal_bf16": [_vp, _u64, _u64, _u32, _u64, _f, _f, _vp],
     "b200_fill_uniform_bf16": [_vp, _u64, _u64, _u32, _u64, _f, _f, _vp],
     "b200_check": [_vp],

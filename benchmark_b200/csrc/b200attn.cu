@@ -324,10 +324,20 @@ void reset_split_counters(int dev) {
       cudaMemset(kv.second.cnt, 0, kv.second.tiles * sizeof(unsigned));
 }
 
+// A caller-fixed split count and workspace (attention_fwd_noalloc).
+struct FixedScratch {
+  int nsplit;            // K/V splits per Q tile; 0: split_count's choice
+  float* o;              // [units][128][128] fp32
+  float2* ml;            // [units][128]
+  unsigned* cnt;         // [Q tiles]
+  size_t max_units, max_qtiles;
+};
+
 template <int D, int EMU, bool TRACE = false>
 b200_status launch_attention(const void* q, const void* k, const void* v, void* o,
                              const AttnShape& s, cudaStream_t stream,
-                             const TraceArgs& tr = TraceArgs{}) {
+                             const TraceArgs& tr = TraceArgs{},
+                             const FixedScratch* fixed = nullptr) {
   using C = b200::attn::Cfg<D>;
   static unsigned attr_done = 0;
   auto kernel = b200::attn::attention_fwd_kernel<D, EMU, TRACE>;
@@ -365,11 +375,27 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   p.n_qtiles = (s.Sq + b200::attn::kBM - 1) / b200::attn::kBM;
   const long long qtiles = static_cast<long long>(pq) * p.n_qtiles;
   const int kv_tiles = (s.Skv + b200::attn::kBN - 1) / b200::attn::kBN;
-  p.nsplit = split_count(qtiles, kv_tiles, sm_count());
+  p.nsplit = (fixed && fixed->nsplit > 0) ? fixed->nsplit : split_count(qtiles, kv_tiles, sm_count());
   const long long items = qtiles * p.nsplit;
   if (items > 0x3fffffffll) return fail(B200_EUNSUPPORTED, "attention: too many work items");
   p.n_items = static_cast<int>(items);
-  if (p.nsplit > 1) {
+  if (p.nsplit > 1 && fixed) {
+    if (static_cast<unsigned long long>(items) > fixed->max_units ||
+        static_cast<unsigned long long>(qtiles) > fixed->max_qtiles)
+      return fail(B200_EUNSUPPORTED,
+                  "attention_fwd_noalloc: %lld split units (%lld Q tiles x %d splits) exceed its "
+                  "fixed scratch of %zu units and %zu Q tiles; pass fewer splits (1 needs no "
+                  "scratch) or use attention_fwd",
+                  items, qtiles, p.nsplit, fixed->max_units, fixed->max_qtiles);
+    // The merge counters must start at zero; a call that failed part-way
+    // may have left counts behind.
+    const cudaError_t e = cudaMemsetAsync(fixed->cnt, 0, static_cast<size_t>(qtiles) *
+                                                             sizeof(unsigned), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "attention_fwd_noalloc: clear merge counters");
+    p.ws_o = fixed->o;
+    p.ws_ml = fixed->ml;
+    p.ws_cnt = fixed->cnt;
+  } else if (p.nsplit > 1) {
     SplitWorkspace w;
     if ((st = split_workspace(stream, static_cast<size_t>(items), static_cast<size_t>(qtiles),
                               &w)) != B200_OK)
@@ -457,6 +483,71 @@ b200_status attention_fwd(const void* q, const void* k, const void* v, void* o, 
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   return D == 128 ? launch_attention<128, kDefaultEmuD128>(q, k, v, o, s, cs)
                   : launch_attention<64, kDefaultEmuD64>(q, k, v, o, s, cs);
+}
+
+}  // extern "C"
+
+// Scratch of attention_fwd_noalloc: the split units' unnormalised O rows
+// (fp32), their per-row (m, l) and the Q tiles' merge counters, in one fixed
+// device array so that the entry point allocates nothing.  Every GPU that
+// loads this library holds it (about 8.1 MiB) until the process exits, and
+// every call shares it: calls that overlap on the GPU (other streams, other
+// host threads) race on it.
+constexpr size_t kNoAllocUnits = 128;   // split units per call (Q tiles x splits)
+constexpr size_t kNoAllocQTiles = 1024; // Q tiles per call when splitting
+constexpr size_t kNoAllocOBytes = kNoAllocUnits * 128 * 128 * sizeof(float);
+constexpr size_t kNoAllocMlBytes = kNoAllocUnits * 128 * sizeof(float2);
+constexpr size_t kNoAllocCntBytes = kNoAllocQTiles * sizeof(unsigned);
+static __device__ __align__(256) unsigned char
+    g_noalloc_scratch[kNoAllocOBytes + kNoAllocMlBytes + kNoAllocCntBytes];
+
+namespace {
+// The array's device address on the current device.  In host code its name
+// is only a host-side stand-in, so the address is looked up once per device
+// (with that device current) and cached.
+b200_status noalloc_scratch(unsigned char** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  constexpr int kMaxDevices = 64;
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(B200_EUNSUPPORTED, "attention_fwd_noalloc: device %d out of range", dev);
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                       "attention_fwd_noalloc: cudaGetSymbolAddress(scratch)");
+    addr[dev] = ptr;
+  }
+  *out = static_cast<unsigned char*>(addr[dev]);
+  return B200_OK;
+}
+}  // namespace
+
+extern "C" {
+
+b200_status attention_fwd_noalloc(const void* q, const void* k, const void* v, void* o, int B,
+                                  int Hq, int Hkv, int Sq, int Skv, int D, int causal,
+                                  float softmax_scale, int nsplit, b200_stream_t stream) {
+  AttnShape s;
+  b200_status st = check_attention_args(q, k, v, o, B, Hq, Hkv, Sq, Skv, D, causal,
+                                        softmax_scale, &s);
+  if (st != B200_OK) return st;
+  if (nsplit < 0 || nsplit > 8)
+    return fail(B200_EINVAL, "attention_fwd_noalloc: nsplit must be 0..8; got %d", nsplit);
+  unsigned char* base = nullptr;
+  if ((st = noalloc_scratch(&base)) != B200_OK) return st;
+  const FixedScratch f{nsplit, reinterpret_cast<float*>(base),
+                       reinterpret_cast<float2*>(base + kNoAllocOBytes),
+                       reinterpret_cast<unsigned*>(base + kNoAllocOBytes + kNoAllocMlBytes),
+                       kNoAllocUnits, kNoAllocQTiles};
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  return D == 128 ? launch_attention<128, kDefaultEmuD128>(q, k, v, o, s, cs, TraceArgs{}, &f)
+                  : launch_attention<64, kDefaultEmuD64>(q, k, v, o, s, cs, TraceArgs{}, &f);
 }
 
 b200_status attention_fwd_trace(const void* q, const void* k, const void* v, void* o, int B,

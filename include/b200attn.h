@@ -67,6 +67,33 @@ b200_status attention_fwd(const void* q, const void* k, const void* v, void* o, 
                           b200_stream_t stream);
 
 /*
+ * attention_fwd for callers that cannot allocate device memory: it runs the
+ * same kernel, but when it splits a short problem's K/V range among several
+ * CTAs their partial results meet in a fixed scratch array compiled into
+ * this library instead of a workspace allocated with cudaMalloc.  Meant for
+ * plugin hosts that own all device memory through their own pool and
+ * forbid other allocations, and for latency-bound callers that cannot take
+ * cudaMalloc's device-wide synchronisation.  The caller still passes every
+ * input and output; nothing is allocated.
+ *   nsplit: K/V splits per 128-row Q tile, 1..8; 1 uses no scratch (any
+ *   size); 0 picks the same split as attention_fwd.
+ *   Limit: when splitting, at most 128 split units (Q tiles x nsplit) and
+ *   1024 Q tiles per call; larger requests return B200_EUNSUPPORTED with a
+ *   message naming the limit.
+ *   The scratch (about 8.1 MiB) is held by every GPU that loads the library
+ *   until the process exits, and is shared by all calls: calls that overlap
+ *   on the GPU (other streams or threads) race and must be serialised by the
+ *   caller.  Each call clears the merge counters it uses before its kernel.
+ *   The first call on a device looks up the array's device address there
+ *   (cudaGetSymbolAddress) and caches it; make that first call before any
+ *   stream capture.
+ * This entry point has no counterpart in the reference.
+ */
+b200_status attention_fwd_noalloc(const void* q, const void* k, const void* v, void* o, int B,
+                                  int Hq, int Hkv, int Sq, int Skv, int D, int causal,
+                                  float softmax_scale, int nsplit, b200_stream_t stream);
+
+/*
  * attention_fwd with clock-cycle tracing of one CTA (diagnostics; runs the
  * default exp2 split).  trace: device buffer of 6 * trace_cap * 2 uint64
  * (zero it first).  Role r (0 Q/K TMA producer, 1 MMA issuer, 2 and 3 the
