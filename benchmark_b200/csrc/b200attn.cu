@@ -234,16 +234,12 @@ b200_status check_attention_args(const void* q, const void* k, const void* v, co
   return B200_OK;
 }
 
-// FMA-pipe exp2 share (pairs of every 8) per head_dim (compile-time; the
-// build may override the defaults with -DB200_ATTN_EMU_D128= / _D64=).
-#ifndef B200_ATTN_EMU_D128
-#define B200_ATTN_EMU_D128 0
-#endif
-#ifndef B200_ATTN_EMU_D64
-#define B200_ATTN_EMU_D64 1
-#endif
-constexpr int kDefaultEmuD128 = B200_ATTN_EMU_D128;
-constexpr int kDefaultEmuD64 = B200_ATTN_EMU_D64;
+// FMA-pipe exp2 share (pairs of every 8) per head_dim.  Measured on B200
+// (c2: d128, c4: d64 workloads): none for d128, whose softmax tile is bound
+// by its control latencies rather than MUFU (one pair in eight lost 1.6 %),
+// and one pair in eight for d64, where MUFU is the tighter pipe.
+constexpr int kDefaultEmuD128 = 0;
+constexpr int kDefaultEmuD64 = 1;
 
 struct TraceArgs {
   unsigned long long* buf = nullptr;
@@ -720,7 +716,7 @@ b200::gemm::Params gemm_params(int M, int N, int K, int b_col_major, void* C, in
 
 // Raster group (256-row blocks per group), measured on B200 (B [K,N]): groups
 // of 8 are best at 8192^3 (16 costs 0.4 %), groups of 16 at 16384^3 (+2 %
-// over 8).
+// over 8; groups of 4 or 32 read 30-50 % more from DRAM).
 int gemm_default_group(int K) { return K >= 12288 ? 16 : 8; }
 
 // Clusters of two that can be resident at once on the current device.

@@ -152,8 +152,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
   if (warp == kTmaWarp) {
     // ================= TMA producer (both CTAs) =================
     if (lane == 0) {
-      // evict_last on both operands (evict_first or evict_normal on either
-      // measured 1-10 % slower on B200)
+      // evict_last on both operands: on B200 evict_normal / evict_first read
+      // 8 % / 100 % more from DRAM at 8192^3 and 29 % / 92 % more at 16384^3
+      // and ran slower
       const uint64_t pol = l2_policy_evict_last();
       const uint64_t pol_b = pol;
       const int group = p.group_m > 0 ? p.group_m : kGroupM;
