@@ -69,14 +69,14 @@ WORKLOADS = {
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel
 # of each workload, from the ncu captures summarised in profiles/ (None: not
-# captured).  c3 and c4 were captured on their 8-GPU shards (8 heads; batch 8)
-# and are scaled to the full problem by its items (the traffic grows with
-# them: each group of 8 planes, or each batch, streams its own K/V once).
+# captured).  c4 was captured on its 8-GPU shard (batch 8) and is scaled to
+# the full problem by its items (the traffic grows with them: each batch
+# streams its own K/V once); c3 was captured on the full 64-head problem.
 NCU_TRAFFIC_BYTES = {
-    "c2": 514.84e6,     # profiles/attention_fwd_d128_c2_b4h32n4096.md
+    "c2": 514.55e6,     # profiles/attention_fwd_d128_c2_b4h32n4096.md
     "c1": 6.37e6,       # profiles/attention_fwd_d128_c1_b1h8n1024.md
-    "c3": 8 * 193.92e6,  # profiles/attention_fwd_d128_c3_causal_h8n16384.md
-    "c4": 8 * 110.97e6,  # profiles/attention_fwd_d64_c4_b8h16n2048.md
+    "c3": 3.06e9,       # profiles/attention_fwd_d128_c3_causal_h64n16384_l2.md
+    "c4": 8 * 109.19e6,  # profiles/attention_fwd_d64_c4_b8h16n2048.md
     "gemm": 1152.5e6,   # profiles/gemm_bf16_pair_8192_b_row_major.md
     "gemm16k": 20.78e9,  # profiles/gemm_bf16_pair_16384_b_col_major.md (B [N,K] capture)
 }
@@ -605,7 +605,9 @@ def measure_gemm(key: str, args, ranks: Ranks, stream, peaks, peak_src, steps: i
 
 
 def public(entry: dict) -> dict:
-    return {k: v for k, v in entry.items() if not k.startswith("_")}
+    out = {k: v for k, v in entry.items() if not k.startswith("_")}
+    out["idle_before_s"] = CONFIG_IDLE_S
+    return out
 
 
 def run_e2e(args, part, q, k, v, o, stream, ranks: Ranks, flops) -> dict:
@@ -619,6 +621,14 @@ def run_e2e(args, part, q, k, v, o, stream, ranks: Ranks, flops) -> dict:
                          ranks.barrier, flops)
 
 
+# Idle time before each extra workload.  A B200 under its 1 kW cap lowers its
+# SM clock after a few tens of ms of dense work and recovers within a fraction
+# of a second of idling; without the pause each workload would inherit the
+# clock the previous one left behind (the config-4 line read 458 TFLOP/s right
+# after config 3 and 665 on a rested GPU).
+CONFIG_IDLE_S = 1.0
+
+
 def strong_and_configs(args, ranks: Ranks, stream, peaks, peak_src, main_key: str) -> tuple:
     """The `strong` object (every N) and the `configs` object (N=1 only)."""
     steps = max(3, min(args.steps, args.config_steps))
@@ -626,7 +636,9 @@ def strong_and_configs(args, ranks: Ranks, stream, peaks, peak_src, main_key: st
     for key in ("c3", "c4"):
         if args.no_configs:
             break
-        r = measure_attention(key, args, ranks, stream, peaks, peak_src, steps, 3)
+        time.sleep(CONFIG_IDLE_S)
+        r = measure_attention(key, args, ranks, stream, peaks, peak_src, steps, 3,
+                              with_clocks=True)
         strong[key] = {"workload": r["workload"], "value": r["value"], "unit": r["unit"],
                        "ms_per_step": r["ms_per_step"], "per_rank": r["per_rank"],
                        "split": "heads" if WORKLOADS[key]["split"] == "h" else "batch",
@@ -640,7 +652,9 @@ def strong_and_configs(args, ranks: Ranks, stream, peaks, peak_src, main_key: st
                 continue
             fn = measure_gemm if WORKLOADS[key].get("kind") == "gemm" else measure_attention
             csteps = steps if key != "c1" else max(steps, 50)
-            configs[key] = public(fn(key, args, ranks, stream, peaks, peak_src, csteps, 3))
+            time.sleep(CONFIG_IDLE_S)
+            configs[key] = public(fn(key, args, ranks, stream, peaks, peak_src, csteps, 3,
+                                     with_clocks=True))
     return strong, configs
 
 

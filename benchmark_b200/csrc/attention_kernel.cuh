@@ -76,9 +76,10 @@ constexpr int kBM = 128;  // query rows per work item (= TMEM lanes)
 constexpr int kBN = 128;  // keys per K/V tile
 constexpr int kEpiWarp0 = 8;
 constexpr int kTmaWarp = 12;   // Q and K loads
-constexpr int kMmaWarp = 13;
+constexpr int kMmaWarp = 13;   // O += P V issuer
 constexpr int kTmaVWarp = 14;  // V loads
-constexpr int kThreads = 512;  // warp 15 only completes warpgroup 3
+constexpr int kMmaSWarp = 15;  // S = Q K^T issuer
+constexpr int kThreads = 512;
 // Registers per thread after the split: softmax warpgroups 0-1 grow, the
 // epilogue warpgroup 2 and the producer/issuer warpgroup 3 shrink; the sum is
 // the pool the block launches with (512 threads x 128).
@@ -106,7 +107,6 @@ struct Params {
   int causal;      // bottom-right aligned
   int causal_off;  // Skv - Sq
   int cgroup;      // causal: Q planes per ordering group (their K/V fit in L2 together)
-  int kv_evict_first;  // L2 policy of the K/V loads: 1 evict_first, 0 evict_last
   // Split K/V ranges (short sequences): each Q tile's K/V tiles are divided
   // among nsplit work units; a unit writes its unnormalised O rows and (m, l)
   // to ws_o / ws_ml, and the last unit of a Q tile to finish (ws_cnt) merges
@@ -118,8 +118,8 @@ struct Params {
   float scale_log2;  // softmax_scale * log2(e)
   // Clock trace (kTrace instantiations only): per-role record regions of
   // trace_cap records (2 x u64: (event << 32 | tile << 24 | iter), clock64)
-  // for CTA trace_cta.  Role r (0 Q/K TMA, 1 MMA, 2/3 softmax warps 0 and 4,
-  // 4 epilogue, 5 V TMA) starts at trace + r * trace_cap * 2.
+  // for CTA trace_cta.  Role r (0 Q/K TMA, 1 PV issuer, 2/3 softmax warps 0
+  // and 4, 4 epilogue, 5 V TMA, 6 S issuer) starts at trace + r * trace_cap * 2.
   unsigned long long* trace;
   int trace_cap;
   int trace_cta;
@@ -129,9 +129,10 @@ struct Params {
 enum : uint32_t {
   kEvTmaK = 1, kEvTmaV, kEvTmaQ, kEvMmaS, kEvMmaPv, kEvMmaWait, kEvMmaGo, kEvMmaEnd, kEvSmWait,
   kEvSmReady, kEvSmLdDone, kEvSmMaxDone, kEvSmPComputed, kEvSmPublished, kEvSmItemEnd,
-  kEvEpiBegin, kEvEpiEnd
+  kEvEpiBegin, kEvEpiEnd, kEvSmPLoopDone
 };
-constexpr int kTraceRoles = 6;  // 0 K/Q TMA, 1 MMA, 2/3 softmax warps 0/4, 4 epilogue, 5 V TMA
+// 0 K/Q TMA, 1 PV issuer, 2/3 softmax warps 0/4, 4 epilogue, 5 V TMA, 6 S issuer
+constexpr int kTraceRoles = 7;
 
 template <bool kTrace>
 struct Tracer {
@@ -173,8 +174,8 @@ struct Cfg {
   static constexpr int kFlagOff = kLOff + 128 * 8;  // abort flag and merge flag (epilogue)
   static constexpr int kBarOff = kFlagOff + 16;
   // q_full[2] q_empty[2] k_full[K] k_empty[K] v_full[V] v_empty[V]
-  // s_ready[3] p_ready[3] pv_done o_full o_empty l_ready[2] drain done
-  static constexpr int kNumBars = 4 + 2 * kKStages + 2 * kVStages + 2 * kSBufs + 1 + 4 + 2;
+  // s_ready[3] p_ready[3] p_free[3] pv_done o_full o_empty l_ready[2] drain done
+  static constexpr int kNumBars = 4 + 2 * kKStages + 2 * kVStages + 3 * kSBufs + 1 + 4 + 2;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kTmemSlotOff + 16 + 1024;  // + 1 KiB alignment slack
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB of shared memory a CTA may use");
@@ -335,7 +336,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_empty = v_full + C::kVStages;
   uint64_t* s_ready = v_empty + C::kVStages;
   uint64_t* p_ready = s_ready + kSBufs;
-  uint64_t* pv_done = p_ready + kSBufs;
+  uint64_t* p_free = p_ready + kSBufs;  // PV(t) done: S buffer t % kSBufs reusable
+  uint64_t* pv_done = p_free + kSBufs;
   uint64_t* o_full = pv_done + 1;
   uint64_t* o_empty = o_full + 1;
   uint64_t* l_ready = o_empty + 1;
@@ -357,6 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kSBufs; ++i) {
       mbar_init(&s_ready[i], 1);
       mbar_init(&p_ready[i], 8);
+      mbar_init(&p_free[i], 1);
     }
     mbar_init(o_full, 1);
     mbar_init(o_empty, 128);
@@ -369,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_empty[s], 1);
     }
     mbar_init(pv_done, 1);
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);  // one commit from each MMA issuer
     mbar_init(done, 1);
     mbar_arrive(done);
     abort_flag[0] = 0;
@@ -394,16 +397,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Each warpgroup moves its register budget first, inside its own branch,
   // so the compiler sizes each role's code to that role's budget.
   if (warp >= static_cast<uint32_t>(kTmaWarp)) {
-    // Warpgroup 3: producers and MMA issuer (warp 15 only completes the group).
+    // Warpgroup 3: producers and the two MMA issuers.
     setmaxnreg_dec<kCtlRegs>();
     if (warp == kTmaWarp || warp == kTmaVWarp) {
       // ================= TMA producers (Q + K, and V) =================
       if (lane == 0) {
         const bool is_k = warp == kTmaWarp;
         Tracer<kTrace> tr(p, is_k ? 0 : 5, trace_cta);
+        // Q is read once; K/V tiles are re-read by every Q tile of their
+        // plane while they sit in L2.
         const uint64_t pol_q = l2_policy_evict_first();
-        const uint64_t pol_kv =
-            p.kv_evict_first ? l2_policy_evict_first() : l2_policy_evict_last();
+        const uint64_t pol_kv = l2_policy_evict_last();
         int t = 0, li = 0, issued = 0, q_issued = -1;
         bool ok = true;
         for (int r = 0; r < rounds && ok; ++r) {
@@ -463,12 +467,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __syncwarp();
-    } else if (warp == kMmaWarp) {
-      // ================= MMA issuer =================
-      // The whole warp runs this loop (operands stay warp-uniform); one elected
-      // lane issues each MMA and commit.
+    } else if (warp == kMmaWarp || warp == kMmaSWarp) {
+      // ================= MMA issuers =================
+      // Warp 15 issues S = Q K^T, warp 13 issues O += P V.  Each warp runs its
+      // loop whole (operands stay warp-uniform) and one elected lane issues
+      // each MMA and commit.  Two issuers keep the tensor pipe fed while one
+      // of them waits on a barrier: measured with peak_probe --probe tile, a
+      // single warp issuing the kernel's per-tile stream (8 SS + 8 TS MMAs,
+      // four commits, a grouped barrier test before each group) needs 1,289
+      // cycles per tile, two warps 1,024 = the MMAs alone.  A commit tracks
+      // only its own thread's MMAs, so each warp signals its own barriers,
+      // and the S issuer learns that PV(t) has read P(t) (S buffer t % 3
+      // free for S(t+3)) from p_free rather than from issue order.
       {
-        Tracer<kTrace> tr(p, 1, trace_cta && lane == 0);
+        const bool is_pv = warp == kMmaWarp;
+        Tracer<kTrace> tr(p, is_pv ? 1 : 6, trace_cta && lane == 0);
         const uint32_t q_addr = smem_u32(q_buf);
         const uint32_t k_addr = smem_u32(k_buf);
         const uint32_t v_addr = smem_u32(v_buf);
@@ -493,116 +506,81 @@ __global__ void __launch_bounds__(kThreads, 1)
           tr(kEvMmaGo, site, 0);
           return true;
         };
-        // S(t) = Q[qb] K(t)^T into S buffer t % kSBufs.
-        auto issue_s = [&](int t_, int qb) {
-          tr(kEvMmaS, qb, t_);
-          const uint64_t dq = dq0 + qb * kTile16;
-          const uint64_t dk = dk0 + (t_ % C::kKStages) * kTile16;
-          const uint32_t ts = tmem_base + static_cast<uint32_t>((t_ % kSBufs) * 128);
-  #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kBox16 + (kk & 3) * 2;
-            mma_ss_warp(ts, dq + off, dk + off, C::kIdescS, kk > 0 ? 1u : 0u);
-          }
-          mma_commit_warp(&k_empty[t_ % C::kKStages]);
-          mma_commit_warp(&s_ready[t_ % kSBufs]);
-        };
-        // O (+)= P(t)[keys 64*half ...] V(t)[keys 64*half ...]
-        auto issue_pv_half = [&](int t_, bool first, int half) {
-          if (half == 0) tr(kEvMmaPv, 0, t_);
-          const uint64_t dv = dv0 + (t_ % C::kVStages) * kTile16;
-          const uint32_t tp = tmem_base + static_cast<uint32_t>((t_ % kSBufs) * 128);
-  #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
-            const int kk = half * 4 + k4;
-            mma_ts_warp(tO, tp + kk * 8, dv + kk * (2048 >> 4), C::kIdescO,
-                        (!first || kk > 0) ? 1u : 0u);
-          }
-        };
-        // Next valid round after r (rounds if none).
-        auto next_round = [&](int r) {
-          for (++r; r < rounds; ++r)
-            if (item_index(p, r) < p.n_items) break;
-          return r;
-        };
-
-        // S cursor: the next S to issue, up to kSBufs - 1 tiles ahead of the
-        // PV cursor and never beyond the item after the PV cursor's (the Q of
-        // a later item waits for an epilogue that waits for this thread).
-        int s_r = next_round(-1), s_li = 0, s_j = 0, s_t = 0;
-        Item s_it{};
-        auto s_settle = [&]() {  // move past items without K/V tiles
-          while (s_r < rounds) {
-            s_it = decode_item(p, item_index(p, s_r));
-            if (s_it.n > 0) break;
-            s_r = next_round(s_r);
-            ++s_li;
-          }
-        };
-        s_settle();
-        auto issue_s_upto = [&](int limit_t, int max_li) -> bool {
-          while (s_r < rounds && s_t <= limit_t && s_li <= max_li) {
-            const int qb = s_li & 1;
-            if (s_j == 0 &&
-                !wait3(bar(&q_full[qb]), static_cast<uint32_t>(s_li >> 1) & 1u, dn_a, dn_p, dn_a,
-                       dn_p, kSiteQFull))
-              return false;
-            if (!wait3(bar(&k_full[s_t % C::kKStages]), kpar(s_t), dn_a, dn_p, dn_a, dn_p,
-                       kSiteKFull))
-              return false;
-            issue_s(s_t, qb);
-            ++s_t;
-            if (++s_j == s_it.n) {
-              s_j = 0;
-              s_r = next_round(s_r);
-              ++s_li;
-              s_settle();
-            }
-          }
-          return true;
-        };
-
-        // PV cursor.
         int t = 0, li = 0;
         bool ok = true;
-        for (int r = next_round(-1); r < rounds && ok; r = next_round(r), ++li) {
-          const Item it = decode_item(p, item_index(p, r));
-          const uint32_t oe_par = (static_cast<uint32_t>(li) & 1u) ^ 1u;  // epilogue of li-1
-          if (it.n == 0) {
-            // No K/V tiles: O stays unwritten (the epilogue stores zeros in Q's
-            // buffer, so Q(li) must have landed first).
-            ok = wait3(bar(&q_full[li & 1]), static_cast<uint32_t>(li >> 1) & 1u, bar(o_empty),
-                       oe_par, dn_a, dn_p, kSiteQFull);
+        if (!is_pv) {
+          // S(t) = Q[qb] K(t)^T into S buffer t % kSBufs, once K(t) has landed
+          // and PV(t - kSBufs) has consumed that buffer's P.
+          for (int r = 0; r < rounds && ok; ++r) {
+            const int k = item_index(p, r);
+            if (k >= p.n_items) continue;
+            const Item it = decode_item(p, k);
+            const int qb = li & 1;
+            const uint32_t qpar = static_cast<uint32_t>(li >> 1) & 1u;
+            ++li;
+            if (it.n == 0) continue;
+            ok = wait3(bar(&q_full[qb]), qpar, dn_a, dn_p, dn_a, dn_p, kSiteQFull);
+            const uint64_t dq = dq0 + qb * kTile16;
+            for (int j = 0; j < it.n && ok; ++j, ++t) {
+              const int sb = t % kSBufs;
+              ok = wait3(bar(&k_full[t % C::kKStages]), kpar(t), bar(&p_free[sb]),
+                         (static_cast<uint32_t>(t / kSBufs) & 1u) ^ 1u, dn_a, dn_p, kSiteKFull);
+              if (!ok) break;
+              tr(kEvMmaS, qb, t);
+              const uint64_t dk = dk0 + (t % C::kKStages) * kTile16;
+              const uint32_t ts = tmem_base + static_cast<uint32_t>(sb * 128);
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t off = (kk >> 2) * kBox16 + (kk & 3) * 2;
+                mma_ss_warp(ts, dq + off, dk + off, C::kIdescS, kk > 0 ? 1u : 0u);
+              }
+              mma_commit_warp(&k_empty[t % C::kKStages]);
+              mma_commit_warp(&s_ready[sb]);
+            }
+          }
+        } else {
+          for (int r = 0; r < rounds && ok; ++r) {
+            const int k = item_index(p, r);
+            if (k >= p.n_items) continue;
+            const Item it = decode_item(p, k);
+            const uint32_t oe_par = (static_cast<uint32_t>(li) & 1u) ^ 1u;  // epilogue of li-1
+            if (it.n == 0) {
+              // No K/V tiles: O stays unwritten (the epilogue stores zeros in Q's
+              // buffer, so Q(li) must have landed first).
+              ok = wait3(bar(&q_full[li & 1]), static_cast<uint32_t>(li >> 1) & 1u, bar(o_empty),
+                         oe_par, dn_a, dn_p, kSiteQFull);
+              if (!ok) break;
+              mma_commit_warp(o_full);
+              ++li;
+              continue;
+            }
+            for (int j = 0; j < it.n && ok; ++j, ++t) {
+              const int sb = t % kSBufs;
+              // V(t), P(t) and, for an item's first tile, O free (the epilogue
+              // of item li-1 has read it), in one grouped wait.
+              ok = wait3(bar(&v_full[t % C::kVStages]), vpar(t), bar(&p_ready[sb]),
+                         static_cast<uint32_t>(t / kSBufs) & 1u, j == 0 ? bar(o_empty) : dn_a,
+                         j == 0 ? oe_par : dn_p, kSitePReady);
+              if (!ok) break;
+              tr(kEvMmaPv, 0, t);
+              // O (+)= P(t) V(t): P is read from the S buffer as the A operand.
+              const uint64_t dv = dv0 + (t % C::kVStages) * kTile16;
+              const uint32_t tp = tmem_base + static_cast<uint32_t>(sb * 128);
+#pragma unroll
+              for (int kk = 0; kk < kBN / 16; ++kk)
+                mma_ts_warp(tO, tp + kk * 8, dv + kk * (2048 >> 4), C::kIdescO,
+                            (j > 0 || kk > 0) ? 1u : 0u);
+              mma_commit_warp(&v_empty[t % C::kVStages]);
+              mma_commit_warp(&p_free[sb]);
+              mma_commit_warp(pv_done);
+            }
             if (!ok) break;
             mma_commit_warp(o_full);
-            continue;
+            ++li;
           }
-          for (int j = 0; j < it.n && ok; ++j) {
-            const int tt = t + j;
-            const uint32_t tpar = static_cast<uint32_t>(tt / kSBufs) & 1u;
-            ok = issue_s_upto(tt + kSBufs - 1, li + 1);
-            if (!ok) break;
-            if (j == 0) {
-              // O is free once the epilogue of item li-1 has read it.
-              ok = wait3(bar(o_empty), oe_par, dn_a, dn_p, dn_a, dn_p, kSiteOEmpty);
-              if (!ok) break;
-            }
-            // One grouped wait per PV: polls cost a few hundred cycles each,
-            // and S(t+2), issued just before, keeps the tensor pipe busy
-            // meanwhile.
-            ok = wait3(bar(&v_full[tt % C::kVStages]), vpar(tt), bar(&p_ready[tt % kSBufs]), tpar,
-                       dn_a, dn_p, kSitePReady);
-            if (!ok) break;
-            issue_pv_half(tt, j == 0, 0);
-            issue_pv_half(tt, j == 0, 1);
-            mma_commit_warp(&v_empty[tt % C::kVStages]);
-            mma_commit_warp(pv_done);
-          }
-          if (!ok) break;
-          mma_commit_warp(o_full);
-          t += it.n;
         }
-        // Every MMA issued above has completed once this commit lands.
+        // Every MMA this warp issued has completed once its commit lands
+        // (the barrier counts one commit from each issuer).
         mma_commit_warp(drain);
         drain_wait(drain, 0);
         tr(kEvMmaEnd, 0, t);
@@ -730,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_16x128b_x8(tS + 32 * half, pk);
           }
           ready = mbar_try_wait(smem_u32(&s_ready[nb]), static_cast<uint32_t>((tt + 1) / kSBufs) & 1u);
-          tr(kEvSmMaxDone, warp >> 2, tt);
+          tr(kEvSmPLoopDone, warp >> 2, tt);
           // Some x of the tile exceeds kRescaleLog2 only if some P value
           // exceeds kRescaleP, and then so does the sum of its lane (all terms
           // are non-negative): the partial sums screen for the rare case, and
@@ -914,6 +892,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = static_cast<int>(quad * 32 + lane);
     const uint32_t lane_addr = (quad * 32u) << 16;
     Tracer<kTrace> tr(p, 4, trace_cta && quad == 0 && lane == 0);
+    // O is never read back: stored evict_first, its dirty lines do not crowd
+    // K/V out of L2.  Measured on config 3 in full (64 causal heads of
+    // 16384): without the hint the L2 filled with O lines and K/V came from
+    // HBM 6x over (18.9 GB per launch against 3.1 GB with it), and the power
+    // that cost lowered the clock under the 1 kW cap.
+    const uint64_t pol_o = l2_policy_evict_first();
     int li = 0;
 #pragma unroll 1
     for (int r = 0; r < rounds; ++r) {
@@ -1091,7 +1075,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (quad == 0 && lane == 0) {
         if (store) {
           for (int b = 0; b < C::kBoxes; ++b)
-            tma_store_3d(&o_map, obuf + b * C::kBoxBytes, b * 64, it.row0, it.zq);
+            tma_store_3d_hint(&o_map, obuf + b * C::kBoxBytes, b * 64, it.row0, it.zq, pol_o);
           bulk_commit_group();
           bulk_wait_group_read<0>();
         }

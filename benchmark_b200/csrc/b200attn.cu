@@ -403,18 +403,16 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   p.causal = s.causal;
   p.causal_off = s.Skv - s.Sq;
   // Causal items are ordered in groups of planes whose K/V (shared by the
-  // group's query heads under GQA) fit in about half of the 126 MB L2, and
-  // their K/V loads are marked evict_first; non-causal items of one head are
-  // adjacent and keep evict_last.  Measured on B200 at interleaved, equal
-  // clocks: config 3 in full (64 heads, N=16384) ~25 % faster than one
-  // heaviest-first order over all heads with evict_last; configs 2 and 4
-  // within noise of either policy.
+  // group's query heads under GQA) fit in about half of the 126 MB L2, so the
+  // CTAs running at one time share their K/V there.  Measured on B200 at
+  // interleaved, equal clocks (with evict_first K/V loads and O stores
+  // without a hint, the policies of the time): config 3 in full (64 heads,
+  // N=16384) ~25 % faster than one heaviest-first order over all heads.
   {
     const double kv_bytes = 4.0 * static_cast<double>(s.Skv) * D;  // K + V of one kv plane
     const double budget = 64.0 * (1 << 20);
     const long long g = static_cast<long long>(budget / kv_bytes) * p.group;
     p.cgroup = static_cast<int>(std::max<long long>(1, std::min<long long>(g, pq)));
-    p.kv_evict_first = s.causal;
   }
   p.scale_log2 = s.scale * 1.4426950408889634f;
   p.trace = tr.buf;

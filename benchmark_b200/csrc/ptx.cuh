@@ -276,6 +276,16 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
       : "memory");
 }
 
+// The same store with an L2 eviction-priority hint (a createpolicy value).
+__device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap* map, const void* src, int x,
+                                                  int y, int z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group.L2::cache_hint"
+      " [%0, {%2, %3, %4}], [%1], %5;" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -747,6 +757,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// 16-byte global store with an L2 eviction-priority hint (a createpolicy value).
+__device__ __forceinline__ void st_global_v4_hint(void* ptr, uint32_t a, uint32_t b, uint32_t c,
+                                                  uint32_t d, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(a),
+               "r"(b), "r"(c), "r"(d), "l"(policy)
+               : "memory");
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,

@@ -4,7 +4,7 @@
 // 2.TMEM_LDST (TMEM load/store rate) and the exp/MUFU rate its softmax
 // design assumes, plus a plain HBM copy:
 //
-//   peak_probe [--probe mma|issue|tmem|mufu|hbm|all] [--iters N] [--device N]
+//   peak_probe [--probe mma|issue|tile|tmem|mufu|hbm|all] [--iters N] [--device N]
 //
 // One CTA per SM.  Each probe prints one line `probe=... value=... unit=...`
 // with the per-SM cycle count behind it.  Operand values do not matter for a
@@ -190,6 +190,106 @@ __global__ void __launch_bounds__(128) mma_issue_probe(int issuers, int reuse, i
   }
 }
 
+// The attention kernel's per-tile MMA stream for d=128: S = Q K^T as eight
+// M128 N128 K16 SS MMAs into one of three 128-column S buffers (Q and K
+// 128 x 128 bf16, K-major SW128 in two 64-column boxes), then O += P V as
+// eight M128 N128 K16 TS MMAs with P read from that S buffer and V (keys x D,
+// MN-major SW128) from shared memory, O in columns 384-511.  mode:
+//   0  one issuing warp, MMAs only
+//   1  one issuing warp, plus the kernel's four commits per tile
+//   2  one issuing warp, commits, and before each group the kernel's grouped
+//      barrier test (three try_waits, warp vote, fence) on phases that have
+//      already completed
+//   3  two issuing warps (S groups / PV groups), each with its commits and
+//      grouped test before each of its groups
+//   4  two issuing warps, MMAs only
+// Values are whatever the operands hold (timing only).
+__global__ void __launch_bounds__(128, 1) tile_issue_probe(int mode, int iters,
+                                                           unsigned long long* cycles) {
+  extern __shared__ uint8_t raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  constexpr uint32_t kBox = 16384, kTile = 32768;
+  uint8_t* q = smem;
+  uint8_t* k = smem + kTile;
+  uint8_t* v = smem + 2 * kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 3 * kTile);  // 0 final, 1-4 commits, 5 idle
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + 3 * kTile + 64);
+  const int issuers = mode >= 3 ? 2 : 1;
+  for (int i = threadIdx.x; i < 3 * static_cast<int>(kTile) / 4; i += blockDim.x)
+    reinterpret_cast<uint32_t*>(smem)[i] = 0x3f803f80u ^ (static_cast<uint32_t>(i) & 0x000f000fu);
+  fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], static_cast<uint32_t>(issuers));
+    for (int b = 1; b < 6; ++b) mbar_init(&bars[b], 1);
+    fence_mbar_init();
+  }
+  if (warp_id() == 0) {
+    tmem_alloc(slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  const unsigned long long t0 = clock64();
+  const int w = static_cast<int>(warp_id());
+  if (w < issuers) {
+    constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
+    constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, false, true);
+    const uint64_t dq = sdesc_sw128(smem_u32(q), 16, 1024);
+    const uint64_t dk = sdesc_sw128(smem_u32(k), 16, 1024);
+    const uint64_t dv = sdesc_sw128(smem_u32(v), kBox, 1024);
+    const uint32_t idle = smem_u32(&bars[5]);
+    const bool do_s = issuers == 1 || w == 0;
+    const bool do_pv = issuers == 1 || w == 1;
+    const bool commits = mode == 1 || mode == 2 || mode == 3;
+    const bool waits = mode == 2 || mode == 3;
+    bool ok = true;
+    for (int t = 0; t < iters && ok; ++t) {
+      const uint32_t sbuf = tmem + static_cast<uint32_t>((t % 3) * 128);
+      if (do_s) {
+        if (waits) {
+          ok = __all_sync(0xffffffffu, mbar_wait3(idle, 1u, idle, 1u, idle, 1u, 0x54));
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * (kBox >> 4) + (kk & 3) * 2;
+          mma_ss_warp(sbuf, dq + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        if (commits) {
+          mma_commit_warp(&bars[1]);
+          mma_commit_warp(&bars[2]);
+        }
+      }
+      if (do_pv) {
+        if (waits) {
+          ok = ok && __all_sync(0xffffffffu, mbar_wait3(idle, 1u, idle, 1u, idle, 1u, 0x55));
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ts_warp(tmem + 384u, sbuf + kk * 8, dv + kk * (2048 >> 4), idesc_o, 1u);
+        if (commits) {
+          mma_commit_warp(&bars[3]);
+          mma_commit_warp(&bars[4]);
+        }
+      }
+    }
+    mma_commit_warp(&bars[0]);
+  }
+  const bool ok = mbar_wait(&bars[0], 0, 0x56);
+  const unsigned long long t1 = clock64();
+  if (threadIdx.x == 0) cycles[blockIdx.x] = ok ? t1 - t0 : 0ull;
+  tc_fence_before();
+  __syncthreads();
+  if (warp_id() == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // tcgen05.ld / tcgen05.st 32x32b.x32 by four warps (each its lane quadrant).
 __global__ void __launch_bounds__(128, 1) tmem_probe(int store, int iters,
                                                      unsigned long long* cycles,
@@ -297,7 +397,7 @@ int main(int argc, char** argv) {
       return argv[++i];
     };
     if (f == "--help") {
-      std::printf("peak_probe [--probe mma|issue|tmem|mufu|hbm|all] [--iters N] [--device N]\n");
+      std::printf("peak_probe [--probe mma|issue|tile|tmem|mufu|hbm|all] [--iters N] [--device N]\n");
       return 0;
     } else if (f == "--probe") probe = next();
     else if (f == "--iters") iters = std::atoi(next());
@@ -308,7 +408,7 @@ int main(int argc, char** argv) {
     }
   }
   if (iters < 16 || iters > (1 << 20) ||
-      (probe != "mma" && probe != "issue" && probe != "tmem" && probe != "mufu" &&
+      (probe != "mma" && probe != "issue" && probe != "tile" && probe != "tmem" && probe != "mufu" &&
        probe != "hbm" && probe != "all")) {
     std::fprintf(stderr, "invalid arguments (see --help)\n");
     return 2;
@@ -405,6 +505,22 @@ int main(int argc, char** argv) {
                       flops / (ms * 1e-3) / 1e12, ms);
         }
       }
+    }
+  }
+  if (probe == "tile" || probe == "all") {
+    cudaFuncSetAttribute(tile_issue_probe, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kSmemProbe);
+    const char* names[5] = {"mma_only", "commits", "commits_waits", "two_issuers_commits_waits",
+                            "two_issuers_mma_only"};
+    const int tiles = iters / 4 > 16 ? iters / 4 : 16;
+    for (int mode = 0; mode < 5; ++mode) {
+      const double ms = timed([&] {
+        tile_issue_probe<<<sms, 128, kSmemProbe>>>(mode, tiles, cyc);
+      });
+      const double per_tile = mean_cycles(cyc, sms) / tiles;
+      const double flops = 4.0 * 128 * 128 * 128 * tiles * sms;
+      std::printf("probe=tile_issue_d128_%s cycles_per_tile=%.1f value=%.1f unit=TFLOP/s "
+                  "ms=%.4f\n", names[mode], per_tile, flops / (ms * 1e-3) / 1e12, ms);
     }
   }
   if (probe == "tmem" || probe == "all") {

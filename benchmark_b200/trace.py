@@ -10,8 +10,9 @@ reference's per-iteration CSV, which its plotter renders to SVG.
     python -m benchmark_b200.trace --b 4 --h 32 --n 4096 --d 128 --cta 7 \\
         --csv trace.csv --reference-csv trace_ref.csv
 
-Records carry the CTA's global K/V tile index as `iter` (tile t belongs to
-softmax pipe t & 1); softmax records carry the pipe as `tile`.
+Records carry the CTA's global K/V tile index as `iter`; every softmax warp
+works on every tile, and softmax records carry the warpgroup (0 or 1) of the
+traced warp as `tile`.
 """
 from __future__ import annotations
 
@@ -23,8 +24,11 @@ from collections import defaultdict
 EVENTS = {1: "tma_k", 2: "tma_v", 3: "tma_q", 4: "mma_s", 5: "mma_pv", 6: "mma_wait",
           7: "mma_go", 8: "mma_end", 9: "sm_wait", 10: "sm_ready", 11: "sm_ld_done",
           12: "sm_max_done", 13: "sm_p_computed", 14: "sm_published", 15: "sm_item_end",
-          16: "epi_begin", 17: "epi_end"}
-ROLES = {0: "tma", 1: "mma", 2: "softmax0", 3: "softmax1", 4: "epilogue", 5: "tma_v"}
+          16: "epi_begin", 17: "epi_end", 18: "sm_p_loop_done"}
+ROLES = {0: "tma", 1: "mma", 2: "softmax0", 3: "softmax1", 4: "epilogue", 5: "tma_v", 6: "mma_qk"}
+# The traced softmax warps: warp 0 (role softmax0) and warp 4 (role softmax1).
+SOFTMAX_ROLES = ("softmax0", "softmax1")
+SOFTMAX_WARP = {"softmax0": 0, "softmax1": 4}
 
 
 def run_trace(q, k, v, causal=False, cta=0, cap=16384, raise_on_timeout=True):
@@ -77,29 +81,42 @@ def _index(recs):
 
 
 def summarize(recs):
-    """Median per-tile stage lengths (cycles) of both softmax pipes, their
-    period, and the issuer's reaction time to a published P."""
+    """Median per-tile stage lengths (cycles) of the two traced softmax warps
+    (warp 0 of the first softmax warpgroup, warp 4 of the second; all eight
+    softmax warps work on every K/V tile), their period, and the issuer's
+    reaction time to a published P.
+
+    Per tile t of a warp: wait_s (sm_wait -> sm_ready), ld (the score load),
+    then for a tile whose P is computed against the running max and screened
+    (the common case) p_loop (exp2, pack and P stores) and screen (P-sum
+    screen and S(t+1) readiness vote), or for a first or masked tile max (the
+    exact tile max) and p_loop_exact; publish (store wait, fence, arrive),
+    busy (sm_ready -> published) and period (sm_wait(t) -> sm_wait(t+1))."""
     at = _index(recs)
     stages = defaultdict(list)
-    for pipe in (0, 1):
-        role = f"softmax{pipe}"
+    for role in SOFTMAX_ROLES:
         iters = sorted({r["iter"] for r in recs if r["role"] == role and r["event"] == "sm_wait"})
         for t in iters:
             g = {e: at.get((role, e, t)) for e in
-                 ("sm_wait", "sm_ready", "sm_ld_done", "sm_max_done", "sm_p_computed",
-                  "sm_published")}
+                 ("sm_wait", "sm_ready", "sm_ld_done", "sm_p_computed", "sm_published")}
             if None in g.values():
                 continue
             stages[f"{role}.wait_s"].append(g["sm_ready"] - g["sm_wait"])
             stages[f"{role}.ld"].append(g["sm_ld_done"] - g["sm_ready"])
-            stages[f"{role}.max"].append(g["sm_max_done"] - g["sm_ld_done"])
-            stages[f"{role}.p_loop"].append(g["sm_p_computed"] - g["sm_max_done"])
+            loop_done = at.get((role, "sm_p_loop_done", t))
+            max_done = at.get((role, "sm_max_done", t))
+            if loop_done is not None:
+                stages[f"{role}.p_loop"].append(loop_done - g["sm_ld_done"])
+                stages[f"{role}.screen"].append(g["sm_p_computed"] - loop_done)
+            elif max_done is not None:
+                stages[f"{role}.max"].append(max_done - g["sm_ld_done"])
+                stages[f"{role}.p_loop_exact"].append(g["sm_p_computed"] - max_done)
             stages[f"{role}.publish"].append(g["sm_published"] - g["sm_p_computed"])
             stages[f"{role}.busy"].append(g["sm_published"] - g["sm_ready"])
-            nxt = at.get((role, "sm_wait", t + 2))
+            nxt = at.get((role, "sm_wait", t + 1))
             if nxt is not None:
                 stages[f"{role}.period"].append(nxt - g["sm_wait"])
-            s_issue = at.get(("mma", "mma_s", t))
+            s_issue = at.get(("mma_qk", "mma_s", t))
             if s_issue is not None:
                 stages[f"{role}.s_issue_to_ready"].append(g["sm_ready"] - s_issue)
             pv = at.get(("mma", "mma_pv", t))
@@ -142,51 +159,51 @@ def reference_rows(recs, elapsed_ms: float = 0.0, clock_offset: int = 1) -> list
     The reference's stages map onto this kernel's as follows (a stage this
     kernel does not have, or does not stamp, is written as 0, which the
     reference plotter treats as absent):
-      tma    K(t) load issued -> S(t) issued (the issuer had seen K(t) land)
-      mma    S(t) issued -> its softmax pipe saw S(t) complete
+      tma    K(t) load issued -> S(t) issued (the S issuer had seen K(t) land)
+      mma    S(t) issued -> softmax warp 0 saw S(t) complete
       ld     that moment -> the scores are in registers (tcgen05.ld done)
-      pack   -> P computed (row max, exp2, bf16 pack and P stores issued)
+      pack   -> P computed (exp2, bf16 pack, P stores issued, screen)
       st     -> P published (store wait, fence, barrier arrive)
       v_tma  V(t) load issued -> PV(t) issued
-      pv     PV(t) issued -> the next MMA issued after it
-    `pipe` is the softmax pipe (t & 1).  Warp ids follow the plotter's lane
-    model, one lane set per pipe (0.attention/plot_attention_trace.py:339-396):
-    warp_id = pv_warp_id = pipe (its "QK/PV warp" lane: this kernel's MMA
-    issuer, warp 13, serving that pipe), tma_warp_id = 2 + pipe (its "K/V
-    TMA" lane: warps 12 and 14 here), and the traced softmax warp (warp 0 or
-    4 here) as consumer lane 0 of its pipe.  Clocks are shifted by
-    clock_offset so that no stamp is 0."""
+      pv     PV(t) issued -> the PV issuer's next record (its MMAs accepted)
+    The kernel has one pipe: its eight softmax warps all work on every tile
+    (16 rows each), so every row has pipe 0.  Warp ids follow the plotter's
+    lane model (0.attention/plot_attention_trace.py:339-396): warp_id =
+    pv_warp_id = 0 (its "QK/PV warp" lane: this kernel's MMA issuers, warps
+    15 and 13), tma_warp_id = 2 (its "K/V TMA" lane: warps 12 and 14 here), and
+    the two traced softmax warps, 0 and 4, as consumer lanes 0 and 4 of the
+    eight.  Clocks are shifted by clock_offset so that no stamp is 0."""
     at = _index(recs)
-    mma_issue = sorted((r["clock"], r["event"], r["iter"]) for r in recs
-                       if r["role"] == "mma" and r["event"] in ("mma_s", "mma_pv"))
-    next_issue = {}
-    for (_, e0, i0), (c1, _, _) in zip(mma_issue, mma_issue[1:]):
-        next_issue[(e0, i0)] = c1
-    tiles = sorted({r["iter"] for r in recs if r["role"] in ("softmax0", "softmax1")
-                    and r["event"] == "sm_published"})
+    pv_warp = sorted((r["clock"], r["event"], r["iter"]) for r in recs if r["role"] == "mma")
+    pv_issued = {}  # PV(t) issued -> the PV issuer's next record (its 8 MMAs accepted)
+    for (_, e0, i0), (c1, _, _) in zip(pv_warp, pv_warp[1:]):
+        if e0 == "mma_pv":
+            pv_issued[i0] = c1
+    lead = SOFTMAX_ROLES[0]
+    tiles = sorted({r["iter"] for r in recs if r["role"] == lead and r["event"] == "sm_published"})
     rows = []
     for t in tiles:
-        pipe = t & 1
-        role = f"softmax{pipe}"
-
         def g(role_, ev, it=t):
             return at.get((role_, ev, it))
 
+        def consumer(role_):
+            return {"ld": (g(role_, "sm_ready"), g(role_, "sm_ld_done")),
+                    "pack": (g(role_, "sm_ld_done"), g(role_, "sm_p_computed")),
+                    "st": (g(role_, "sm_p_computed"), g(role_, "sm_published"))}
+
         stamps = {
-            "tma": (g("tma", "tma_k"), g("mma", "mma_s")),
-            "mma": (g("mma", "mma_s"), g(role, "sm_ready")),
-            "ld": (g(role, "sm_ready"), g(role, "sm_ld_done")),
-            "pack": (g(role, "sm_ld_done"), g(role, "sm_p_computed")),
-            "st": (g(role, "sm_p_computed"), g(role, "sm_published")),
+            "tma": (g("tma", "tma_k"), g("mma_qk", "mma_s")),
+            "mma": (g("mma_qk", "mma_s"), g(lead, "sm_ready")),
+            **consumer(lead),
             "v_tma": (g("tma_v", "tma_v"), g("mma", "mma_pv")),
-            "pv": (g("mma", "mma_pv"), next_issue.get(("mma_pv", t))),
+            "pv": (g("mma", "mma_pv"), pv_issued.get(t)),
         }
         row = {c: 0 for c in REFERENCE_COLUMNS}
-        row.update({"mode": "b200_two_pipe_attention_trace", "elapsed_ms": f"{elapsed_ms:.6f}",
-                    "iter": t, "pipe": pipe, "warp_id": pipe, "tma_warp_id": 2 + pipe,
-                    "pv_warp_id": pipe, "pv_h0_warp_id": -1, "pv_h1_warp_id": -1,
+        row.update({"mode": "b200_attention_trace", "elapsed_ms": f"{elapsed_ms:.6f}",
+                    "iter": t, "pipe": 0, "warp_id": 0, "tma_warp_id": 2,
+                    "pv_warp_id": 0, "pv_h0_warp_id": -1, "pv_h1_warp_id": -1,
                     "status": "ok", "cuda_error": "no error",
-                    "notes": "stages mapped onto the two-pipe kernel (benchmark_b200/trace.py)"})
+                    "notes": "stages mapped onto the one-pipe kernel (benchmark_b200/trace.py)"})
         first = last = None
         for name, (a, b) in stamps.items():
             if a is None or b is None or b < a:
@@ -198,10 +215,13 @@ def reference_rows(recs, elapsed_ms: float = 0.0, clock_offset: int = 1) -> list
             last = b if last is None else max(last, b)
         if row["tma_start"] == 0:  # the plotter's time base is the rows' tma_start
             continue
-        for name in ("ld", "pack", "st"):
-            if row[f"{name}_start"]:
-                row[f"{name}_warp0_start"] = row[f"{name}_start"]
-                row[f"{name}_warp0_end"] = row[f"{name}_end"]
+        for role in SOFTMAX_ROLES:
+            lane = SOFTMAX_WARP[role]
+            for name, (a, b) in consumer(role).items():
+                if a is None or b is None or b < a:
+                    continue
+                row[f"{name}_warp{lane}_start"] = a + clock_offset
+                row[f"{name}_warp{lane}_end"] = b + clock_offset
         row["total_start"] = first + clock_offset
         row["total_end"] = last + clock_offset
         row["total_cycles"] = last - first

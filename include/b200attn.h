@@ -95,9 +95,9 @@ b200_status attention_fwd_noalloc(const void* q, const void* k, const void* v, v
 
 /*
  * attention_fwd with clock-cycle tracing of one CTA (diagnostics; runs the
- * default exp2 split).  trace: device buffer of 6 * trace_cap * 2 uint64
- * (zero it first).  Role r (0 Q/K TMA producer, 1 MMA issuer, 2 and 3 the
- * softmax pipes 0 and 1 (their first warps), 4 epilogue, 5 V TMA producer)
+ * default exp2 split).  trace: device buffer of 7 * trace_cap * 2 uint64
+ * (zero it first).  Role r (0 Q/K TMA producer, 1 PV MMA issuer, 2 and 3
+ * softmax warps 0 and 4, 4 epilogue, 5 V TMA producer, 6 S MMA issuer)
  * writes up to trace_cap records at trace + r*trace_cap*2, each
  * {(event << 32) | (tile << 24) | iteration, clock64()}; the iteration of
  * TMA, MMA and softmax records is the CTA's global K/V tile index.  Events

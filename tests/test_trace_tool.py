@@ -18,21 +18,23 @@ ROOT = Path(__file__).resolve().parents[1]
 
 
 def _recs(tiles=8):
-    """A synthetic two-pipe trace: tile t on pipe t & 1, one period 2000
-    cycles per pipe, pipe 1 half a period behind."""
+    """A synthetic trace: one tile every 2000 cycles, both traced softmax
+    warps on every tile (warp 4 30 cycles behind warp 0), the first tile
+    taking the exact-max path and the rest the screened path."""
     recs = []
     for t in range(tiles):
-        pipe = t & 1
-        base = 1000 * t + 1000
+        base = 2000 * t + 1000
         recs.append({"role": "tma", "event": "tma_k", "tile": 0, "iter": t, "clock": base - 900})
         recs.append({"role": "tma_v", "event": "tma_v", "tile": 0, "iter": t, "clock": base - 800})
-        recs.append({"role": "mma", "event": "mma_s", "tile": 0, "iter": t, "clock": base - 600})
-        recs.append({"role": "mma", "event": "mma_pv", "tile": pipe, "iter": t,
-                     "clock": base + 1300})
-        for ev, dt in (("sm_wait", -100), ("sm_ready", 0), ("sm_ld_done", 150),
-                       ("sm_max_done", 250), ("sm_p_computed", 1050), ("sm_published", 1250)):
-            recs.append({"role": f"softmax{pipe}", "event": ev, "tile": pipe, "iter": t,
-                         "clock": base + dt})
+        recs.append({"role": "mma_qk", "event": "mma_s", "tile": 0, "iter": t, "clock": base - 600})
+        recs.append({"role": "mma", "event": "mma_pv", "tile": 0, "iter": t, "clock": base + 1300})
+        recs.append({"role": "mma", "event": "mma_wait", "tile": 4, "iter": 0, "clock": base + 1400})
+        mid = ("sm_max_done", 250) if t == 0 else ("sm_p_loop_done", 950)
+        for wg, lag in ((0, 0), (1, 30)):
+            for ev, dt in (("sm_wait", -100), ("sm_ready", 0), ("sm_ld_done", 150), mid,
+                           ("sm_p_computed", 1050), ("sm_published", 1250)):
+                recs.append({"role": f"softmax{wg}", "event": ev, "tile": wg, "iter": t,
+                             "clock": base + dt + lag})
     return recs
 
 
@@ -40,13 +42,16 @@ def test_summarize_stage_lengths():
     st = trace.summarize(_recs())
     assert st["softmax0.wait_s"][0] == 100
     assert st["softmax0.ld"][0] == 150
-    assert st["softmax0.max"][0] == 100
-    assert st["softmax0.p_loop"][0] == 800
+    assert st["softmax0.p_loop"][0] == 800 and st["softmax0.p_loop"][3] == 7
+    assert st["softmax0.screen"][0] == 100
+    assert st["softmax0.max"] == (100, 100, 100, 1)  # the first tile only
+    assert st["softmax0.p_loop_exact"][0] == 800
     assert st["softmax0.publish"][0] == 200
     assert st["softmax1.busy"][0] == 1250
-    assert st["softmax0.period"][0] == 2000 and st["softmax0.period"][3] == 3
-    assert st["softmax1.s_issue_to_ready"][0] == 600
+    assert st["softmax0.period"][0] == 2000 and st["softmax0.period"][3] == 7
+    assert st["softmax1.s_issue_to_ready"][0] == 630
     assert st["mma.softmax0_published_to_pv_issue"][0] == 50
+    assert st["mma.softmax1_published_to_pv_issue"][0] == 20
 
 
 def _kernel_event_count():
@@ -57,7 +62,7 @@ def _kernel_event_count():
 
 
 def test_event_and_role_tables_cover_the_kernel_enums():
-    # One name per event the kernel's Tracer writes (1..n) and roles 0..5.
+    # One name per event the kernel's Tracer writes (1..n) and per role.
     assert sorted(trace.EVENTS) == list(range(1, _kernel_event_count() + 1))
     src = (Path(trace.__file__).parent / "csrc" / "attention_kernel.cuh").read_text()
     roles = int(re.search(r"constexpr int kTraceRoles = (\d+);", src).group(1))
@@ -84,12 +89,16 @@ def test_reference_csv_columns_and_stages(tmp_path):
         rows = list(csv.DictReader(f))
     assert list(rows[0].keys()) == trace.REFERENCE_COLUMNS
     r3 = rows[3]
-    assert int(r3["iter"]) == 3 and int(r3["pipe"]) == 1
+    assert int(r3["iter"]) == 3 and int(r3["pipe"]) == 0
     assert int(r3["ld_cycles"]) == 150 and int(r3["pack_cycles"]) == 900
     assert int(r3["st_cycles"]) == 200 and int(r3["mma_cycles"]) == 600
     assert int(r3["tma_cycles"]) == 300 and int(r3["v_tma_cycles"]) == 2100
-    assert int(r3["ld_warp0_start"]) == int(r3["ld_start"])  # the pipe's traced warp
-    assert int(r3["warp_id"]) == 1 and int(r3["tma_warp_id"]) == 3
+    assert int(r3["pv_cycles"]) == 100  # PV(3) issued -> the PV issuer's next wait
+    assert int(r3["ld_warp0_start"]) == int(r3["ld_start"])  # warp 0 is consumer lane 0
+    assert int(r3["ld_warp4_start"]) == int(r3["ld_start"]) + 30  # warp 4 is lane 4
+    assert int(r3["st_warp4_end"]) == int(r3["st_end"]) + 30
+    assert int(r3["ld_warp1_start"]) == 0  # untraced lanes stay empty
+    assert int(r3["warp_id"]) == 0 and int(r3["tma_warp_id"]) == 2
     assert all(int(r["tma_start"]) > 0 for r in rows)
 
 
