@@ -16,6 +16,7 @@
 #include "b200attn.h"
 #include "ptx.cuh"
 #include "attention_kernel.cuh"
+#include "attention_pair_kernel.cuh"
 #include "reference_kernels.cuh"
 #include "gemm_kernel.cuh"
 
@@ -329,6 +330,36 @@ struct FixedScratch {
   size_t max_units, max_qtiles;
 };
 
+// The two-Q-tile d=64 kernel on already encoded maps (64-column boxes of 128
+// rows, as launch_attention encodes them for d=64).
+template <int EMU>
+b200_status launch_pair(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+                        const CUtensorMap& om, b200::attn::Params p, long long units,
+                        cudaStream_t stream) {
+  namespace pa = b200::attn::pair;
+  static unsigned attr_done = 0;
+  auto kernel = pa::attention_pair_kernel<EMU>;
+  b200_status st = ensure_smem_attr(kernel, pa::kSmemBytes, &attr_done);
+  if (st != B200_OK) return st;
+  static const int launch_regs = [kernel] {
+    cudaFuncAttributes a{};
+    return cudaFuncGetAttributes(&a, kernel) == cudaSuccess ? a.numRegs : -1;
+  }();
+  if (launch_regs != b200::attn::kLaunchRegs)
+    return fail(B200_EUNSUPPORTED,
+                "attention (d=64 pairs): kernel has %d registers per thread at launch; its "
+                "register split needs exactly %d",
+                launch_regs, b200::attn::kLaunchRegs);
+  if (units > 0x3fffffffll) return fail(B200_EUNSUPPORTED, "attention: too many work units");
+  p.n_items = static_cast<int>(units);
+  p.nsplit = 1;
+  const int grid = static_cast<int>(std::min<long long>(units, sm_count()));
+  kernel<<<grid, b200::attn::kThreads, pa::kSmemBytes, stream>>>(qm, km, vm, om, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attention_fwd launch (d=64 pairs)");
+  return B200_OK;
+}
+
 template <int D, int EMU, bool TRACE = false>
 b200_status launch_attention(const void* q, const void* k, const void* v, void* o,
                              const AttnShape& s, cudaStream_t stream,
@@ -402,6 +433,14 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   }
   p.causal = s.causal;
   p.causal_off = s.Skv - s.Sq;
+  p.scale_log2 = s.scale * 1.4426950408889634f;
+  if constexpr (D == 64 && !TRACE) {
+    // Non-causal d=64 problems that fill the GPU without a K/V split run two
+    // Q tiles per work unit (attention_pair_kernel.cuh).
+    const long long units = static_cast<long long>(pq) * ((p.n_qtiles + 1) / 2);
+    if (!s.causal && p.nsplit == 1 && units >= sm_count())
+      return launch_pair<EMU>(qm, km, vm, om, p, units, stream);
+  }
   // Causal items are ordered in groups of planes whose K/V (shared by the
   // group's query heads under GQA) fit in about half of the 126 MB L2, so the
   // CTAs running at one time share their K/V there.  Measured on B200 at
@@ -414,7 +453,6 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
     const long long g = static_cast<long long>(budget / kv_bytes) * p.group;
     p.cgroup = static_cast<int>(std::max<long long>(1, std::min<long long>(g, pq)));
   }
-  p.scale_log2 = s.scale * 1.4426950408889634f;
   p.trace = tr.buf;
   p.trace_cap = tr.cap;
   p.trace_cta = tr.cta;
