@@ -13,12 +13,12 @@
 //               32*(w%4) + 16*(w/4) + [0,16)), four threads per row
 //   warps 8-11  epilogue: O / l -> bf16 -> shared -> TMA store
 //   warp  12    TMA producer for Q (per item) and the K ring; TMEM allocator
-//   warp  13    tcgen05.mma issuer (whole warp, one elected lane issues)
+//   warp  13    O += P V issuer (whole warp, one elected lane issues)
 //   warp  14    TMA producer for the V ring (its own thread, so K loads run
 //               ahead of the V ring's slower turnover)
-//   warp  15    idle; it completes warpgroup 3, so that each warpgroup can
-//               move its register budget with setmaxnreg (softmax 184,
-//               epilogue 64, producers/issuer 80 registers per thread)
+//   warp  15    S = Q K^T issuer
+// Each warpgroup moves its register budget with setmaxnreg (softmax 184,
+// epilogue 64, producers/issuers 80 registers per thread).
 //
 // TMEM (512 columns): three S buffers [0,128) [128,256) [256,384) rotate over
 // the global tile sequence; O at [384, 384+D).  P (bf16 pairs) overwrites the
@@ -35,11 +35,12 @@
 // tile apart; eight independent softmax warps (16 rows each) put two on
 // every scheduler without any cross-warp barrier.
 //
-// MMA issue order over the global tile stream t (crossing item boundaries):
-//   S(0), S(1), then for every t: S(t+2), PV(t)   (PV(t) issued once all
-//   eight softmax warps have stored P(t)).  S(t+3) overwrites P(t) after
-//   PV(t) in issue order; the tensor pipe executes one thread's MMAs in
-//   issue order.
+// MMA issue over the global tile stream t (crossing item boundaries): warp
+// 15 issues S(t) once K(t) has landed and PV(t-3) has completed (p_free: P(t-3)
+// lives in the buffer S(t) overwrites); warp 13 issues PV(t) once all eight
+// softmax warps have stored P(t) and V(t) has landed.  Two issuers keep the
+// tensor pipe fed while one of them waits on a barrier (a single warp issuing
+// both streams measured 26 % slower in isolation, peak_probe --probe tile).
 //
 // Softmax per tile: a thread reads 32 scores of each of its two rows
 // (16x256b TMEM loads); where a row max is needed it is completed by two
