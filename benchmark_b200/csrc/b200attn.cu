@@ -736,8 +736,7 @@ extern "C" b200_status b200_selftest_wait_timeout(uint64_t limit_ns, b200_stream
 
 namespace {
 
-b200::gemm::Params gemm_params(int M, int N, int K, int b_col_major, void* C, int bm, int bn,
-                               int bk) {
+b200::gemm::Params gemm_params(int M, int N, int K, int b_col_major, int bm, int bn, int bk) {
   b200::gemm::Params p{};
   p.M = M;
   p.N = N;
@@ -746,7 +745,6 @@ b200::gemm::Params gemm_params(int M, int N, int K, int b_col_major, void* C, in
   p.tiles_n = (N + bn - 1) / bn;
   p.k_blocks = (K + bk - 1) / bk;
   p.b_col_major = b_col_major ? 1 : 0;
-  p.C = static_cast<uint16_t*>(C);
   return p;
 }
 
@@ -793,13 +791,16 @@ b200_status launch_gemm_pair(const void* A, const void* Bm, void* C, int M, int 
   else
     st = encode_bf16_2d(&bm, Bm, N, K, 64, g::pair::kBK);
   if (st != B200_OK) return st;
-  g::Params p = gemm_params(M, N, K, b_col_major, C, g::pair::kBM, g::pair::kBN, g::pair::kBK);
+  CUtensorMap cm;  // C [M, N]: 64-column x 128-row boxes, the epilogue's staging unit
+  if ((st = encode_bf16_2d(&cm, C, N, M, g::pair::kCBoxCols, g::pair::kHalf)) != B200_OK)
+    return st;
+  g::Params p = gemm_params(M, N, K, b_col_major, g::pair::kBM, g::pair::kBN, g::pair::kBK);
   p.group_m = gemm_default_group(K);
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
   if (tiles > 0x3fffffffll) return fail(B200_EUNSUPPORTED, "gemm_bf16: too many tiles");
   const long long clusters = std::min<long long>(tiles, pair_clusters_resident());
   g::gemm_bf16_pair_kernel<<<static_cast<unsigned>(2 * clusters), g::pair::kThreads,
-                             g::pair::kSmemBytes, stream>>>(am, bm, p);
+                             g::pair::kSmemBytes, stream>>>(am, bm, cm, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16 (pair) launch");
   return B200_OK;

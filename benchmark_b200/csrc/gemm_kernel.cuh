@@ -27,7 +27,6 @@ struct Params {
   int tiles_m, tiles_n, k_blocks;
   int b_col_major;  // 1: B is [N,K]; 0: B is [K,N]
   int group_m;      // row blocks per raster group
-  uint16_t* C;
 };
 
 // Tile t -> (m block, n block) in groups of `group` row blocks: a group's
@@ -84,11 +83,19 @@ constexpr uint32_t kTmemCols = 512;  // two accumulators of 256 fp32 columns
 constexpr int kABytes = kHalf * kBK * 2;        // 16 KiB
 constexpr int kBBytes = kHalf * kBK * 2;        // 16 KiB
 constexpr int kStageBytes = kABytes + kBBytes;  // 32 KiB
-constexpr int kBarOff = kStages * kStageBytes;
+// C staging for the TMA stores: two 128-row x 64-column bf16 boxes
+// (128-byte swizzled), used in turn.
+constexpr int kCBoxCols = 64;
+constexpr int kCBoxBytes = kHalf * kCBoxCols * 2;  // 16 KiB
+constexpr int kCStageOff = kStages * kStageBytes;
+constexpr int kBarOff = kCStageOff + 2 * kCBoxBytes;
 constexpr int kNumBars = 2 * kStages + 5;  // full, empty, acc_full[2], acc_empty[2], drain
-constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
+constexpr int kAbortOff = kBarOff + kNumBars * 8;  // epilogue abort flag
+constexpr int kTmemSlotOff = kAbortOff + 16;
 constexpr int kSmemBytes = kTmemSlotOff + 16 + 1024;
+static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB of shared memory a CTA may use");
 constexpr uint32_t kAccEmptyArrivals = 8;  // 4 epilogue warps x 2 CTAs
+constexpr int kBarEpilogue = 1;            // named barrier of the four epilogue warps
 }  // namespace pair
 
 __device__ __forceinline__ void spin_ns(uint64_t ns) {
@@ -98,7 +105,8 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap a_map,
-                          const __grid_constant__ CUtensorMap b_map, const Params p) {
+                          const __grid_constant__ CUtensorMap b_map,
+                          const __grid_constant__ CUtensorMap c_map, const Params p) {
   constexpr int kBM = pair::kBM, kBN = pair::kBN, kHalf = pair::kHalf, kBK = pair::kBK;
   constexpr int kStages = pair::kStages, kTmaWarp = pair::kTmaWarp, kMmaWarp = pair::kMmaWarp;
   constexpr int kGroupM = pair::kGroupM, kABytes = pair::kABytes;
@@ -115,6 +123,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTmemSlotOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + pair::kAbortOff);
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
   const uint32_t rank = cluster_ctarank();
@@ -133,6 +142,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
       mbar_init(&acc_empty[a], pair::kAccEmptyArrivals);
     }
     mbar_init(drain, 1);
+    abort_flag[0] = 0;
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
@@ -142,6 +152,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
   if (warp == kTmaWarp && lane == 0) {
     tma_prefetch_desc(&a_map);
     tma_prefetch_desc(&b_map);
+    tma_prefetch_desc(&c_map);
   }
   // Both CTAs' barriers are initialised before either touches the other's.
   tc_fence_before();
@@ -250,11 +261,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
     const uint32_t quad = warp & 3u;
     const int row = static_cast<int>(quad * 32 + lane);
     const uint32_t lane_addr = (quad * 32u) << 16;
+    const uint32_t sbase = smem_u32(smem + pair::kCStageOff);
+    const bool issuer = warp == 2 && lane == 0;  // issues this CTA's C stores
     // C is never read back: stored evict_first so its lines leave L2 before
     // the A and B panels the next tiles re-read (ncu at 16384^3: DRAM
     // traffic per launch 20.8 GB without the hint, 16.3-16.8 GB with it).
     const uint64_t pol_c = l2_policy_evict_first();
-    int lt = 0;
+    int lt = 0, box = 0;
     for (int t = cluster_id; t < num_tiles; t += num_clusters, ++lt) {
       const int a = lt & 1;
       int mb, nb;
@@ -262,33 +275,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[a],
                                                         static_cast<uint32_t>(lt >> 1) & 1u,
                                                         kSiteAccFull));
-      if (!ok) break;
+      if (!ok) abort_flag[0] = 1;
+      // The four warps leave together: a warp whose wait ran out must not
+      // leave the others at a named barrier.
+      named_bar_sync(pair::kBarEpilogue, 128);
+      if (abort_flag[0] != 0) break;
       tc_fence_after();
-      const int grow = mb * kBM + static_cast<int>(rank) * kHalf + row;
-      uint16_t* crow = p.C + static_cast<size_t>(grow) * p.N;
+      const int grow0 = mb * kBM + static_cast<int>(rank) * kHalf;  // this CTA's first row
+      // Row `row` of this CTA's 128 x 256 block, 64 columns at a time: TMEM
+      // -> bf16 -> the 128-byte-swizzled staging box -> one TMA store (TMA
+      // clips at the edges of C).
 #pragma unroll 1
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(a * kBN + c0), v);
-        tmem_wait_ld(v);
-        uint32_t w[16];
+      for (int c0 = 0; c0 < kBN; c0 += pair::kCBoxCols, ++box) {
+        const uint32_t sb = sbase + static_cast<uint32_t>((box & 1) * pair::kCBoxBytes);
+        if (issuer) bulk_wait_group_read<1>();  // the box's previous store has read it
+        named_bar_sync(pair::kBarEpilogue, 128);
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          w[e] = pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
-        const int gcol = nb * kBN + c0;
-        if (grow < p.M) {
+        for (int h = 0; h < 2; ++h) {
+          uint32_t v[32];
+          tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(a * kBN + c0 + 32 * h), v);
+          tmem_wait_ld(v);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            if (gcol + q * 8 < p.N)
-              st_global_v4_hint(crow + gcol + q * 8, w[4 * q], w[4 * q + 1], w[4 * q + 2],
-                                w[4 * q + 3], pol_c);
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              w[e] = pack_bf16x2(__uint_as_float(v[8 * q + 2 * e]),
+                                 __uint_as_float(v[8 * q + 2 * e + 1]));
+            const int ch = (4 * h + q) ^ (row & 7);
+            st_shared_v4(sb + row * 128 + ch * 16, w[0], w[1], w[2], w[3]);
           }
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(pair::kBarEpilogue, 128);
+        if (issuer) {
+          tma_store_2d_hint(&c_map, smem + pair::kCStageOff + (box & 1) * pair::kCBoxBytes,
+                            nb * kBN + c0, grow0, pol_c);
+          bulk_commit_group();
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[a]), 0));
     }
+    if (issuer) bulk_wait_group<0>();  // every store has completed
   }
 
   // No CTA leaves while its partner may still signal its barriers or read

@@ -276,6 +276,16 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
       : "memory");
 }
 
+// 2-D tile store with an L2 eviction-priority hint (a createpolicy value).
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, const void* src, int x,
+                                                  int y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group.L2::cache_hint"
+      " [%0, {%2, %3}], [%1], %4;" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
 // The same store with an L2 eviction-priority hint (a createpolicy value).
 __device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap* map, const void* src, int x,
                                                   int y, int z, uint64_t policy) {
@@ -757,14 +767,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
-}
-
-// 16-byte global store with an L2 eviction-priority hint (a createpolicy value).
-__device__ __forceinline__ void st_global_v4_hint(void* ptr, uint32_t a, uint32_t b, uint32_t c,
-                                                  uint32_t d, uint64_t policy) {
-  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(a),
-               "r"(b), "r"(c), "r"(d), "l"(policy)
-               : "memory");
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
