@@ -624,8 +624,8 @@ def run_e2e(args, part, q, k, v, o, stream, ranks: Ranks, flops) -> dict:
 # Idle time before each extra workload.  A B200 under its 1 kW cap lowers its
 # SM clock after a few tens of ms of dense work and recovers within a fraction
 # of a second of idling; without the pause each workload would inherit the
-# clock the previous one left behind (the config-4 line read 458 TFLOP/s right
-# after config 3 and 665 on a rested GPU).
+# clock the previous one left behind (with the one-Q-tile kernel, config 4
+# read 458 TFLOP/s right after config 3 and 714 after the pause).
 CONFIG_IDLE_S = 1.0
 
 
