@@ -149,7 +149,7 @@ __device__ __forceinline__ float row_max(const float* s, int valid) {
   return fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3]));
 }
 
-template <int kEmu>
+template <int kEmu, bool kTrace = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_pair_kernel(const __grid_constant__ CUtensorMap q_map,
                           const __grid_constant__ CUtensorMap k_map,
@@ -231,6 +231,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Clock trace (kTrace builds): roles as in the one-Q-tile kernel, the
+  // softmax roles 2 and 3 being pipe A's warp 0 and pipe B's warp 4; MMA and
+  // softmax records carry the S index u as the iteration and the pipe as the
+  // tile.
+  const bool trace_cta = kTrace && static_cast<int>(blockIdx.x) == p.trace_cta;
 
   if (warp >= static_cast<uint32_t>(kTmaWarp)) {
     setmaxnreg_dec<kCtlRegs>();
@@ -238,6 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ================= TMA producers (Q + K, and V) =================
       if (lane == 0) {
         const bool is_k = warp == kTmaWarp;
+        Tracer<kTrace> tr(p, is_k ? 0 : 5, trace_cta);
         const uint64_t pol_q = l2_policy_evict_first();
         const uint64_t pol_kv = l2_policy_evict_last();
         int t = 0, issued = 0, lq0 = 0, lq1 = 0;
@@ -269,6 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = mbar_wait(&k_empty[ks], (static_cast<uint32_t>(t / kKStages) & 1u) ^ 1u,
                              kSiteKEmpty, kDefaultWaitLimitNs, 20000u);
               if (!ok) break;
+              tr(kEvTmaK, 0, t);
               mbar_arrive_expect_tx(&k_full[ks], kTileBytes);
               tma_load_3d(k_buf + ks * kTileBytes, &k_map, &k_full[ks], 0, j * kBN, u.zkv,
                           pol_kv);
@@ -277,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = mbar_wait(&v_empty[vs], (static_cast<uint32_t>(t / kVStages) & 1u) ^ 1u,
                              kSiteVEmpty, kDefaultWaitLimitNs, 20000u);
               if (!ok) break;
+              tr(kEvTmaV, 0, t);
               mbar_arrive_expect_tx(&v_full[vs], kTileBytes);
               tma_load_3d(v_buf + vs * kTileBytes, &v_map, &v_full[vs], 0, j * kBN, u.zkv,
                           pol_kv);
@@ -305,6 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Warp 15 issues S, warp 13 PV, for both pipes in the order S(A,j),
       // S(B,j) / PV(A,j), PV(B,j); u counts the S tiles of the CTA.
       const bool is_pv = warp == kMmaWarp;
+      Tracer<kTrace> tr(p, is_pv ? 1 : 6, trace_cta && lane == 0);
       const uint64_t dq0 = sdesc_sw128(smem_u32(q_buf), 16, 1024);
       const uint64_t dk0 = sdesc_sw128(smem_u32(k_buf), 16, 1024);
       const uint64_t dv0 = sdesc_sw128(smem_u32(v_buf), kTileBytes, 1024);
@@ -336,6 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = wait3(bar(&p_free[sb]), (static_cast<uint32_t>(u / kSBufs) & 1u) ^ 1u, dn_a,
                          dn_p, dn_a, dn_p, kSitePvDone);
               if (!ok) break;
+              tr(kEvMmaS, pp, u);
               const uint64_t dq = dq0 + (2 * pp + (lq[pp] & 1)) * kTile16;
               const uint64_t dk = dk0 + ks * kTile16;
               const uint32_t ts = tmem_base + static_cast<uint32_t>(sb * 128);
@@ -358,6 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          j == 0 ? bar(&o_empty[pp]) : dn_a,
                          j == 0 ? (static_cast<uint32_t>(lq[pp] & 1) ^ 1u) : dn_p, kSitePReady);
               if (!ok) break;
+              tr(kEvMmaPv, pp, u);
               const uint32_t to = tmem_base + kColO + static_cast<uint32_t>(pp * D);
               const uint32_t tp = tmem_base + static_cast<uint32_t>(sb * 128);
               const uint64_t dv = dv0 + vs * kTile16;
@@ -390,6 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = (quad * 32u) << 16;
     const uint32_t tO = tmem_base + lane_addr + kColO + static_cast<uint32_t>(pp * D);
     const float c = p.scale_log2;
+    Tracer<kTrace> tr(p, 2 + pp, trace_cta && quad == 0 && lane == 0);
     int u = 0, tp = 0, lq = 0;
     bool ok = true;
 #pragma unroll 1
@@ -408,9 +420,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int uu = u + j * un.nq + pp;
         const int sb = uu % kSBufs;
         const uint32_t tS = tmem_base + lane_addr + static_cast<uint32_t>(sb * 128);
+        tr(kEvSmWait, pp, uu);
         ok = warp_wait(&s_ready[sb], static_cast<uint32_t>(uu / kSBufs) & 1u, kSiteSReady);
         if (!ok) break;
         tc_fence_after();
+        tr(kEvSmReady, pp, uu);
         uint32_t sr[128];
         tmem_ld_32x32b_x64(tS, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
         tmem_ld_32x32b_x64(tS + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
@@ -418,6 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
         reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
         reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+        tr(kEvSmLdDone, pp, uu);
         const float* s = reinterpret_cast<const float*>(sr);
         const bool masked = j == n - 1 && tail < kBN;
         float f = 1.0f;  // factor on O and l (a rescale)
@@ -425,6 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j == 0 || masked) {
           // Exact row max first (an item's first tile, or the masked tail).
           const float mx = (masked ? row_max<true>(s, tail) : row_max<false>(s, kBN)) * c;
+          tr(kEvSmMaxDone, pp, uu);
           if (m == -INFINITY) {
             m = mx;
           } else if (mx > m + kRescaleLog2) {
@@ -440,6 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // the max by more than 2^kRescaleLog2 (then some P exceeds 2^8, and
           // so does the sum).
           p_row<kEmu, false>(s, c, -m, kBN, tS, ra, rb);
+          tr(kEvSmPLoopDone, pp, uu);
           float e0, e1;
           f2_unpack(f2_add(ra, rb), e0, e1);
           const bool big = e0 + e1 > kRescaleP;
@@ -463,6 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        tr(kEvSmPComputed, pp, uu);
         // O holds this pipe's tiles before j in the old max: rescale it once
         // PV(j-1) has completed (rare; the tile's PV waits for this P).
         if (__any_sync(0xffffffffu, f != 1.0f) && j > 0) {
@@ -490,6 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         mbar_arrive_warp(&p_ready[sb]);
+        tr(kEvSmPublished, pp, uu);
       }
       if (!ok) break;
       u += n * un.nq;

@@ -332,13 +332,13 @@ struct FixedScratch {
 
 // The two-Q-tile d=64 kernel on already encoded maps (64-column boxes of 128
 // rows, as launch_attention encodes them for d=64).
-template <int EMU>
+template <int EMU, bool TRACE>
 b200_status launch_pair(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                         const CUtensorMap& om, b200::attn::Params p, long long units,
                         cudaStream_t stream) {
   namespace pa = b200::attn::pair;
   static unsigned attr_done = 0;
-  auto kernel = pa::attention_pair_kernel<EMU>;
+  auto kernel = pa::attention_pair_kernel<EMU, TRACE>;
   b200_status st = ensure_smem_attr(kernel, pa::kSmemBytes, &attr_done);
   if (st != B200_OK) return st;
   static const int launch_regs = [kernel] {
@@ -434,12 +434,15 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   p.causal = s.causal;
   p.causal_off = s.Skv - s.Sq;
   p.scale_log2 = s.scale * 1.4426950408889634f;
-  if constexpr (D == 64 && !TRACE) {
+  p.trace = tr.buf;
+  p.trace_cap = tr.cap;
+  p.trace_cta = tr.cta;
+  if constexpr (D == 64) {
     // Non-causal d=64 problems that fill the GPU without a K/V split run two
     // Q tiles per work unit (attention_pair_kernel.cuh).
     const long long units = static_cast<long long>(pq) * ((p.n_qtiles + 1) / 2);
     if (!s.causal && p.nsplit == 1 && units >= sm_count())
-      return launch_pair<EMU>(qm, km, vm, om, p, units, stream);
+      return launch_pair<EMU, TRACE>(qm, km, vm, om, p, units, stream);
   }
   // Causal items are ordered in groups of planes whose K/V (shared by the
   // group's query heads under GQA) fit in about half of the 126 MB L2, so the
@@ -453,9 +456,6 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
     const long long g = static_cast<long long>(budget / kv_bytes) * p.group;
     p.cgroup = static_cast<int>(std::max<long long>(1, std::min<long long>(g, pq)));
   }
-  p.trace = tr.buf;
-  p.trace_cap = tr.cap;
-  p.trace_cta = tr.cta;
   // Persistent: one CTA per SM (shared memory admits one), or fewer items.
   const int grid = static_cast<int>(std::min<long long>(items, sm_count()));
   kernel<<<grid, b200::attn::kThreads, C::kSmemBytes, stream>>>(qm, km, vm, om, p);

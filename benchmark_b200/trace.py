@@ -91,8 +91,19 @@ def summarize(recs):
     (the common case) p_loop (exp2, pack and P stores) and screen (P-sum
     screen and S(t+1) readiness vote), or for a first or masked tile max (the
     exact tile max) and p_loop_exact; publish (store wait, fence, arrive),
-    busy (sm_ready -> published) and period (sm_wait(t) -> sm_wait(t+1))."""
+    busy (sm_ready -> published) and period (sm_wait of this tile -> sm_wait of
+    the warp's next tile).  The two-Q-tile kernel (non-causal d=64) records
+    the S index as the iteration and the pipe as the tile; its softmax roles
+    are pipe A's warp 0 and pipe B's warp 4."""
     at = _index(recs)
+    # The role's next tile (t + 1 in the one-Q-tile kernel, the pipe's next S
+    # index in the two-Q-tile kernel).
+    next_wait = {}
+    for role in SOFTMAX_ROLES:
+        waits = sorted((r["iter"], r["clock"]) for r in recs
+                       if r["role"] == role and r["event"] == "sm_wait")
+        for (t0, _), (_, c1) in zip(waits, waits[1:]):
+            next_wait[(role, t0)] = c1
     stages = defaultdict(list)
     for role in SOFTMAX_ROLES:
         iters = sorted({r["iter"] for r in recs if r["role"] == role and r["event"] == "sm_wait"})
@@ -113,7 +124,7 @@ def summarize(recs):
                 stages[f"{role}.p_loop_exact"].append(g["sm_p_computed"] - max_done)
             stages[f"{role}.publish"].append(g["sm_published"] - g["sm_p_computed"])
             stages[f"{role}.busy"].append(g["sm_published"] - g["sm_ready"])
-            nxt = at.get((role, "sm_wait", t + 1))
+            nxt = next_wait.get((role, t))
             if nxt is not None:
                 stages[f"{role}.period"].append(nxt - g["sm_wait"])
             s_issue = at.get(("mma_qk", "mma_s", t))

@@ -100,7 +100,9 @@ b200_status attention_fwd_noalloc(const void* q, const void* k, const void* v, v
  * softmax warps 0 and 4, 4 epilogue, 5 V TMA producer, 6 S MMA issuer)
  * writes up to trace_cap records at trace + r*trace_cap*2, each
  * {(event << 32) | (tile << 24) | iteration, clock64()}; the iteration of
- * TMA, MMA and softmax records is the CTA's global K/V tile index.  Events
+ * TMA, MMA and softmax records is the CTA's global K/V tile index (for
+ * non-causal d=64 problems, traced on the two-Q-tile kernel that runs them:
+ * the S index, with the pipe as the tile field).  Events
  * are listed in benchmark_b200/trace.py, which also writes the reference's
  * per-iteration trace CSV.  Stands in for the reference's
  * ATTENTION_CLOCK_TRACE build and its per-stage CSV
