@@ -98,13 +98,13 @@ __device__ __forceinline__ int unit_index(int r) {
 // P of a 128-key row (s: 128 scores), x = s * sc + nm, stored as bf16 pairs
 // over the first 64 columns at tS (this thread's lane); keys at or past
 // `valid` get exactly 0.  Accumulates the row sum in two packed pairs.
-template <int kEmu, bool kMasked>
+template <int kEmu, bool kMasked, int kC0 = 0, int kC1 = 8>
 __device__ __forceinline__ void p_row(const float* s, float sc, float nm, int valid, uint32_t tS,
                                       uint64_t& ra, uint64_t& rb) {
   const uint64_t sc2 = f2_pack(sc, sc);
   const uint64_t nm2 = f2_pack(nm, nm);
 #pragma unroll
-  for (int c = 0; c < 8; ++c) {
+  for (int c = kC0; c < kC1; ++c) {
     uint32_t pk[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -426,18 +426,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tr(kEvSmReady, pp, uu);
         uint32_t sr[128];
+        const bool masked = j == n - 1 && tail < kBN;
+        const bool exact = j == 0 || masked;
         tmem_ld_32x32b_x64(tS, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
-        tmem_ld_32x32b_x64(tS + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
-        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-        reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-        reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
-        reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+        if (exact) {
+          tmem_ld_32x32b_x64(tS + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
+          tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+          reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+          reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+          reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+        } else {
+          // First half of the scores, then the second half's load runs
+          // under the first half's P.
+          tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+          reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+          tmem_ld_32x32b_x64(tS + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
+        }
         tr(kEvSmLdDone, pp, uu);
         const float* s = reinterpret_cast<const float*>(sr);
-        const bool masked = j == n - 1 && tail < kBN;
         float f = 1.0f;  // factor on O and l (a rescale)
+        bool resc = false;  // some row of the warp rescaled (warp-uniform)
         uint64_t ra = 0ull, rb = 0ull;
-        if (j == 0 || masked) {
+        if (exact) {
           // Exact row max first (an item's first tile, or the masked tail).
           const float mx = (masked ? row_max<true>(s, tail) : row_max<false>(s, kBN)) * c;
           tr(kEvSmMaxDone, pp, uu);
@@ -451,11 +461,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             p_row<kEmu, true>(s, c, -m, tail, tS, ra, rb);
           else
             p_row<kEmu, false>(s, c, -m, kBN, tS, ra, rb);
+          resc = __any_sync(0xffffffffu, f != 1.0f);
         } else {
           // P against the running max; the row's P sum screens for a jump of
           // the max by more than 2^kRescaleLog2 (then some P exceeds 2^8, and
           // so does the sum).
-          p_row<kEmu, false>(s, c, -m, kBN, tS, ra, rb);
+          p_row<kEmu, false, 0, 4>(s, c, -m, kBN, tS, ra, rb);
+          tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+          reg_written_here(*reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+          p_row<kEmu, false, 4, 8>(s, c, -m, kBN, tS, ra, rb);
           tr(kEvSmPLoopDone, pp, uu);
           float e0, e1;
           f2_unpack(f2_add(ra, rb), e0, e1);
@@ -470,7 +484,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 raise = true;
               }
             }
-            if (__any_sync(0xffffffffu, raise)) {
+            resc = __any_sync(0xffffffffu, raise);
+            if (resc) {
               // Redo P against the raised maxima (rows that did not move
               // recompute the same values).
               tmem_wait_st();
@@ -483,7 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tr(kEvSmPComputed, pp, uu);
         // O holds this pipe's tiles before j in the old max: rescale it once
         // PV(j-1) has completed (rare; the tile's PV waits for this P).
-        if (__any_sync(0xffffffffu, f != 1.0f) && j > 0) {
+        if (resc && j > 0) {
           ok = warp_wait(&pv_done[pp], static_cast<uint32_t>(tp - 1) & 1u, kSitePvDone);
           if (!ok) break;
           tc_fence_after();

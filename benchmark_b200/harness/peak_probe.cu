@@ -4,7 +4,7 @@
 // 2.TMEM_LDST (TMEM load/store rate) and the exp/MUFU rate its softmax
 // design assumes, plus a plain HBM copy:
 //
-//   peak_probe [--probe mma|issue|tile|tmem|mufu|hbm|all] [--iters N] [--device N]
+//   peak_probe [--probe mma|issue|tile|tmem|mufu|softmax|hbm|all] [--iters N] [--device N]
 //
 // One CTA per SM.  Each probe prints one line `probe=... value=... unit=...`
 // with the per-SM cycle count behind it.  Operand values do not matter for a
@@ -354,6 +354,101 @@ __global__ void mufu_probe(int iters, unsigned long long* cycles, float* sink) {
   if (threadIdx.x == 0) cycles[blockIdx.x] = t1 - t0;
 }
 
+// The per-element work of the softmax P loop, in pairs, 16 pairs per thread
+// per iteration, 8 warps (two per scheduler, as in the attention kernel):
+//   mode 0  2 ex2
+//   mode 1  2 ex2 + cvt.rn.bf16x2.f32
+//   mode 2  cvt.rn.bf16x2.f32 alone
+//   mode 3  2 ex2 + round-to-nearest-even bf16 packing on the integer pipe
+//   mode 4  the whole pair: fma.f32x2 (scale, subtract max), 2 ex2,
+//           add.f32x2 (row sums), cvt.rn.bf16x2.f32
+//   mode 5  mode 4 with the integer packing of mode 3
+//   mode 6  ex2.approx.ftz.bf16x2 (two bf16 exponentials per instruction)
+//   mode 7  ex2.approx.f16x2
+// Every value is carried from one iteration to the next (ex2 and fma update
+// their own inputs, the cvt of mode 2 feeds its word back as the next input,
+// packed words are folded into one xor), so the assembler can hoist none of
+// them out of the loop.  Elements per cycle per SM = 32 * threads * iters /
+// cycles (pairs of modes 2, 6 and 7 count as 2).
+__device__ __forceinline__ uint32_t probe_pack_rne_int(float a, float b) {
+  // Round-to-nearest-even of two non-negative finite floats to bf16 by
+  // integer arithmetic: add 0x7FFF plus the lowest kept bit, keep the top
+  // halves (bytes 2-3 of each word).
+  const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+  const uint32_t ta = ua + 0x7FFFu + ((ua >> 16) & 1u);
+  const uint32_t tb = ub + 0x7FFFu + ((ub >> 16) & 1u);
+  return __byte_perm(ta, tb, 0x7632);
+}
+
+template <int kMode>
+__global__ void softmax_mix_probe(int iters, unsigned long long* cycles, uint32_t* sink) {
+  float x[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x[i] = -1e-3f * (threadIdx.x + i);
+  uint32_t acc = 0;
+  uint64_t rs = 0;
+  const uint64_t sc2 = (static_cast<uint64_t>(__float_as_uint(0.125f)) << 32) |
+                       __float_as_uint(0.125f);
+  const uint64_t nm2 = (static_cast<uint64_t>(__float_as_uint(-2.0f)) << 32) |
+                       __float_as_uint(-2.0f);
+  __syncthreads();
+  const unsigned long long t0 = clock64();
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float& a = x[2 * j];
+      float& b = x[2 * j + 1];
+      if (kMode == 6 || kMode == 7) {
+        uint32_t r = __float_as_uint(a);
+        if (kMode == 6)
+          asm volatile("ex2.approx.ftz.bf16x2 %0, %0;" : "+r"(r));
+        else
+          asm volatile("ex2.approx.f16x2 %0, %0;" : "+r"(r));
+        a = __uint_as_float(r);
+        continue;
+      }
+      if (kMode == 2) {
+        uint32_t r;
+        asm volatile("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+        a = __uint_as_float(r);
+        continue;
+      }
+      float pa = a, pb = b;
+      if (kMode >= 4) {
+        // s <- s * 0.125 - 2 (carried), p = 2^s
+        uint64_t s2 = (static_cast<uint64_t>(__float_as_uint(b)) << 32) | __float_as_uint(a);
+        asm volatile("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(s2) : "l"(sc2), "l"(nm2));
+        a = __uint_as_float(static_cast<uint32_t>(s2));
+        b = __uint_as_float(static_cast<uint32_t>(s2 >> 32));
+        asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(pa) : "f"(a));
+        asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(pb) : "f"(b));
+        const uint64_t p2 =
+            (static_cast<uint64_t>(__float_as_uint(pb)) << 32) | __float_as_uint(pa);
+        asm volatile("add.rn.f32x2 %0, %0, %1;" : "+l"(rs) : "l"(p2));
+      } else {
+        asm volatile("ex2.approx.ftz.f32 %0, %0;" : "+f"(a));
+        asm volatile("ex2.approx.ftz.f32 %0, %0;" : "+f"(b));
+        pa = a;
+        pb = b;
+      }
+      if (kMode == 1 || kMode == 4) {
+        uint32_t r;
+        asm volatile("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(pb), "f"(pa));
+        acc ^= r;
+      } else if (kMode == 3 || kMode == 5) {
+        acc ^= probe_pack_rne_int(pa, pb);
+      }
+    }
+  }
+  __syncthreads();
+  const unsigned long long t1 = clock64();
+  uint32_t fold = acc ^ static_cast<uint32_t>(rs) ^ static_cast<uint32_t>(rs >> 32);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) fold ^= __float_as_uint(x[i]);
+  sink[blockIdx.x * blockDim.x + threadIdx.x] = fold;
+  if (threadIdx.x == 0) cycles[blockIdx.x] = t1 - t0;
+}
+
 __global__ void copy_probe(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t n) {
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
@@ -397,7 +492,7 @@ int main(int argc, char** argv) {
       return argv[++i];
     };
     if (f == "--help") {
-      std::printf("peak_probe [--probe mma|issue|tile|tmem|mufu|hbm|all] [--iters N] [--device N]\n");
+      std::printf("peak_probe [--probe mma|issue|tile|tmem|mufu|softmax|hbm|all] [--iters N] [--device N]\n");
       return 0;
     } else if (f == "--probe") probe = next();
     else if (f == "--iters") iters = std::atoi(next());
@@ -408,7 +503,7 @@ int main(int argc, char** argv) {
     }
   }
   if (iters < 16 || iters > (1 << 20) ||
-      (probe != "mma" && probe != "issue" && probe != "tile" && probe != "tmem" && probe != "mufu" &&
+      (probe != "mma" && probe != "issue" && probe != "tile" && probe != "tmem" && probe != "mufu" && probe != "softmax" &&
        probe != "hbm" && probe != "all")) {
     std::fprintf(stderr, "invalid arguments (see --help)\n");
     return 2;
@@ -543,6 +638,29 @@ int main(int argc, char** argv) {
     const double ops = 256.0 * 8 * iters;
     std::printf("probe=mufu_ex2_f32 lanes_per_cycle_per_sm=%.2f value=%.1f unit=Gop/s ms=%.4f\n",
                 ops / c, ops * sms / (ms * 1e-3) / 1e9, ms);
+  }
+  if (probe == "softmax" || probe == "all") {
+    static const char* kNames[8] = {"ex2",          "ex2_cvt",      "cvt",
+                                    "ex2_intpack",  "pair_cvt",     "pair_intpack",
+                                    "ex2_bf16x2",   "ex2_f16x2"};
+    for (int mode = 0; mode < 8 && rc == 0; ++mode) {
+      const double ms = timed([&] {
+        switch (mode) {
+          case 0: softmax_mix_probe<0><<<sms, 256>>>(iters, cyc, sink); break;
+          case 1: softmax_mix_probe<1><<<sms, 256>>>(iters, cyc, sink); break;
+          case 2: softmax_mix_probe<2><<<sms, 256>>>(iters, cyc, sink); break;
+          case 3: softmax_mix_probe<3><<<sms, 256>>>(iters, cyc, sink); break;
+          case 4: softmax_mix_probe<4><<<sms, 256>>>(iters, cyc, sink); break;
+          case 5: softmax_mix_probe<5><<<sms, 256>>>(iters, cyc, sink); break;
+          case 6: softmax_mix_probe<6><<<sms, 256>>>(iters, cyc, sink); break;
+          default: softmax_mix_probe<7><<<sms, 256>>>(iters, cyc, sink); break;
+        }
+      });
+      const double c = mean_cycles(cyc, sms);
+      const double elems = 256.0 * 32 * iters;
+      std::printf("probe=softmax_%s elements_per_cycle_per_sm=%.2f value=%.1f unit=Gelem/s "
+                  "ms=%.4f\n", kNames[mode], elems / c, elems * sms / (ms * 1e-3) / 1e9, ms);
+    }
   }
   if (probe == "hbm" || probe == "all") {
     const size_t bytes = static_cast<size_t>(1) << 30;

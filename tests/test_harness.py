@@ -118,7 +118,9 @@ def test_peak_probe_all_runs_with_plausible_rates():
         "issue_m128_n128_ss_same_operands_zeros", "issue_m128_n128_ss_distinct_operands_zeros",
         "tmem_ld_32x32b_x32", "tmem_st_32x32b_x32", "mufu_ex2_f32", "hbm_copy_1GiB"} | {
         "tile_issue_d128_" + m for m in ("mma_only", "commits", "commits_waits",
-                                         "two_issuers_commits_waits", "two_issuers_mma_only")}
+                                         "two_issuers_commits_waits", "two_issuers_mma_only")} | {
+        "softmax_" + m for m in ("ex2", "ex2_cvt", "cvt", "ex2_intpack", "pair_cvt",
+                                 "pair_intpack", "ex2_bf16x2", "ex2_f16x2")}
     assert vals["mma_m128_n256_ss_1acc"] > 500  # TFLOP/s
     assert vals["hbm_copy_1GiB"] > 1000        # GB/s
     assert all(v > 0 for v in vals.values())
