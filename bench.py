@@ -76,7 +76,7 @@ NCU_TRAFFIC_BYTES = {
     "c2": 514.55e6,     # profiles/attention_fwd_d128_c2_b4h32n4096.md
     "c1": 6.37e6,       # profiles/attention_fwd_d128_c1_b1h8n1024.md
     "c3": 3.06e9,       # profiles/attention_fwd_d128_c3_causal_h64n16384_l2.md
-    "c4": 8 * 106.13e6,  # profiles/attention_fwd_d64_c4_b8h16n2048.md
+    "c4": 8 * 107.00e6,  # profiles/attention_fwd_d64_c4_b8h16n2048.md
     "gemm": 1148.0e6,   # profiles/gemm_bf16_pair_8192_b_row_major.md
     "gemm16k": 18.04e9,  # profiles/gemm_bf16_pair_16384_b_row_major.md
 }
