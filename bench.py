@@ -507,10 +507,14 @@ def l2_flusher(dev):
 
 def attention_kernel_name(part: dict) -> str:
     """The kernel the library runs for this workload: non-causal d=64 problems
-    with a unit (two Q tiles) per SM take the two-Q-tile kernel."""
+    with a unit (two Q tiles) per SM take the two-Q-tile kernel; non-causal
+    d=128 problems with a unit per two SMs take the CTA-pair form of the
+    one-Q-tile kernel (cta_group::2, clusters of two)."""
     units = part["b"] * part["h"] * ((part["n"] + 255) // 256)
     if part["d"] == 64 and not part["causal"] and units >= 148:
         return "attention_pair_kernel<1>"
+    if part["d"] == 128 and not part["causal"] and 2 * units >= 148:
+        return "attention_fwd_kernel<128> (CTA pairs, cta_group::2)"
     return f"attention_fwd_kernel<{part['d']}>"
 
 

@@ -158,30 +158,43 @@ struct Tracer {
   }
 };
 
-template <int D>
+// kPair: the CTA-pair form (cta_group::2, non-causal d=128).  Each CTA
+// of a pair holds half of every K tile (64 keys) and half of every V tile (64
+// of its d columns): the pair MMAs take B's N halves from both CTAs, so a
+// K/V tile crosses L2 -> shared memory once per pair of Q tiles, and the
+// halved stages allow deeper rings in the same shared memory.
+template <int D, bool kPair = false>
 struct Cfg {
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
+  static_assert(!kPair || D == 128, "the CTA-pair form is built for head_dim 128");
   static constexpr int kBoxes = D / 64;            // 64-column (128-byte) TMA boxes per tile
   static constexpr int kBoxBytes = 128 * 128;      // 128 rows x 128 B = 16 KiB
   static constexpr int kTileBytes = kBoxes * kBoxBytes;
-  static constexpr int kKStages = (D == 128) ? 3 : 4;  // K ring depth
-  static constexpr int kVStages = (D == 128) ? 2 : 4;  // V ring depth
+  // K stage: kKRows keys x D (kBoxes boxes of kKRows x 128 B); V stage:
+  // 128 keys x kVBoxes 64-column boxes.
+  static constexpr int kKRows = kPair ? 64 : 128;
+  static constexpr int kKBoxBytes = kKRows * 128;
+  static constexpr int kKTileBytes = kBoxes * kKBoxBytes;
+  static constexpr int kVBoxes = kPair ? kBoxes / 2 : kBoxes;
+  static constexpr int kVTileBytes = kVBoxes * kBoxBytes;
+  static constexpr int kKStages = kPair ? 6 : (D == 128) ? 3 : 4;  // K ring depth
+  static constexpr int kVStages = kPair ? 4 : (D == 128) ? 2 : 4;  // V ring depth
   static constexpr int kQOff = 0;                       // Q0, Q1 (also O staging)
   static constexpr int kKOff = 2 * kTileBytes;
-  static constexpr int kVOff = kKOff + kKStages * kTileBytes;
+  static constexpr int kVOff = kKOff + kKStages * kKTileBytes;
   // per-row (m, l) of the item the epilogue works on: one slot suffices, the
   // softmax writes item li's values only after the epilogue released li-1
-  static constexpr int kLOff = kVOff + kVStages * kTileBytes;
+  static constexpr int kLOff = kVOff + kVStages * kVTileBytes;
   static constexpr int kFlagOff = kLOff + 128 * 8;  // abort flag and merge flag (epilogue)
   static constexpr int kBarOff = kFlagOff + 16;
   // q_full[2] q_empty[2] k_full[K] k_empty[K] v_full[V] v_empty[V]
-  // s_ready[3] p_ready[3] p_free[3] pv_done o_full o_empty l_ready[2] drain done
-  static constexpr int kNumBars = 4 + 2 * kKStages + 2 * kVStages + 3 * kSBufs + 1 + 4 + 2;
+  // s_ready[3] p_ready[3] p_free[3] pv_done o_full o_empty l_ready[2] drain done o_free
+  static constexpr int kNumBars = 4 + 2 * kKStages + 2 * kVStages + 3 * kSBufs + 1 + 4 + 3;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kTmemSlotOff + 16 + 1024;  // + 1 KiB alignment slack
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB of shared memory a CTA may use");
-  static constexpr uint32_t kIdescS = idesc_bf16_f32(128, kBN, false, false);
-  static constexpr uint32_t kIdescO = idesc_bf16_f32(128, D, false, true);
+  static constexpr uint32_t kIdescS = idesc_bf16_f32(kPair ? 256 : 128, kBN, false, false);
+  static constexpr uint32_t kIdescO = idesc_bf16_f32(kPair ? 256 : 128, D, false, true);
   static constexpr uint32_t kColO = 128 * kSBufs;
 };
 
@@ -260,6 +273,38 @@ __device__ __forceinline__ int item_index(const Params& p, int r) {
   return r * g + ((p.causal && (r & 1)) ? g - 1 - c : c);
 }
 
+// CTA-pair form (non-causal): work unit k = (plane, pair of adjacent Q
+// tiles); the CTA of cluster rank `rank` takes Q tile 2 * pair + rank (past
+// the last tile when n_qtiles is odd: its rows are out of range, TMA reads
+// zeros and nothing is stored).  Both CTAs visit all K/V tiles of the plane.
+// (Causal problems stay on one CTA per Q tile: pairs there must visit the
+// second tile's extent, whose last tile the first tile's rows mask entirely,
+// and measured 3-5 % slower on config 3.)
+__device__ __forceinline__ Item decode_pair_item(const Params& p, int unit) {
+  // Clusters are (2, 1, 1) over a 1-D grid: the cluster rank is blockIdx.x & 1.
+  const int rank = static_cast<int>(blockIdx.x & 1u);
+  const int npq = (p.n_qtiles + 1) >> 1;
+  const int bh = unit / npq;
+  const int qt = 2 * (unit - bh * npq) + rank;
+  const int b = bh / p.Hq;
+  const int hq = bh - b * p.Hq;
+  Item it;
+  it.zq = bh;
+  it.zkv = b * p.Hkv + hq / p.group;
+  it.row0 = qt * kBM;
+  it.j0 = 0;
+  it.n = (p.Skv + kBN - 1) / kBN;
+  it.min_lim = p.Skv;
+  it.tile = unit;
+  return it;
+}
+
+// The r-th unit of this CTA pair: rounds of (gridDim.x / 2) units.
+__device__ __forceinline__ int pair_item_index(int r) {
+  const int g = static_cast<int>(gridDim.x >> 1);
+  return r * g + static_cast<int>(blockIdx.x >> 1);
+}
+
 // Warp-uniform bounded wait: true only if every lane observed the phase
 // (warp-collective tcgen05.ld/st never run on a partial warp).  Waiting lanes
 // sleep in the hardware wait so they do not take issue slots from others.
@@ -313,13 +358,13 @@ __device__ __forceinline__ void p_rows(const float* s, float sc, float nm_a, flo
   }
 }
 
-template <int D, int kEmu, bool kTrace = false>
+template <int D, int kEmu, bool kTrace = false, bool kPair = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_fwd_kernel(const __grid_constant__ CUtensorMap q_map,
                          const __grid_constant__ CUtensorMap k_map,
                          const __grid_constant__ CUtensorMap v_map,
                          const __grid_constant__ CUtensorMap o_map, const Params p) {
-  using C = Cfg<D>;
+  using C = Cfg<D, kPair>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -344,11 +389,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* l_ready = o_empty + 1;
   uint64_t* drain = l_ready + 2;
   uint64_t* done = drain + 1;  // phase 0 completes at setup and never changes
+  // Pair only, in the leader: both CTAs' epilogues have read O (the PV issuer
+  // may overwrite it).  o_empty stays each CTA's own epilogue -> softmax
+  // handshake.
+  uint64_t* o_free = done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmemSlotOff);
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
-  const int rounds = (p.n_items + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+  // CTA pair: rank 0 (the leader) issues every MMA for both CTAs and owns
+  // the barriers the MMAs wait on (q/k/v_full, p_ready, o_free, p_free);
+  // the barriers the MMAs' commits signal exist in both CTAs.
+  const uint32_t rank = kPair ? (blockIdx.x & 1u) : 0u;  // = %cluster_ctarank for (2, 1, 1)
+  const bool leader = rank == 0;
+  const int units_per_round = static_cast<int>(kPair ? gridDim.x >> 1 : gridDim.x);
+  const int rounds = (p.n_items + units_per_round - 1) / units_per_round;
+  auto item_at = [&](int r) { return kPair ? pair_item_index(r) : item_index(p, r); };
+  auto decode_at = [&](int k) {
+    return kPair ? decode_pair_item(p, k) : decode_item(p, k);
+  };
+  // The leader's copy of a barrier of this CTA's layout (shared::cluster).
+  auto lead_bar = [&](uint64_t* b_) { return mapa_shared(smem_u32(b_), 0u); };
 
   // ---- setup ----
   if (threadIdx.x == 0) {
@@ -359,11 +420,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < kSBufs; ++i) {
       mbar_init(&s_ready[i], 1);
-      mbar_init(&p_ready[i], 8);
+      mbar_init(&p_ready[i], kPair ? 16 : 8);  // softmax warps (of both CTAs)
       mbar_init(&p_free[i], 1);
     }
     mbar_init(o_full, 1);
-    mbar_init(o_empty, 128);
+    mbar_init(o_empty, kPair ? 4 : 128);  // pair: one arrive per epilogue warp
+    mbar_init(o_free, 8);                 // pair: every epilogue warp of both CTAs
     for (int s = 0; s < C::kKStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -381,8 +443,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
   }
   if (warp == kTmaWarp) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
     if (lane == 0) {
       tma_prefetch_desc(&q_map);
       tma_prefetch_desc(&k_map);
@@ -391,7 +458,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   tc_fence_before();
-  __syncthreads();
+  // A pair's barriers are initialised in both CTAs before either signals the
+  // other's.
+  if constexpr (kPair)
+    cluster_sync_all();
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const bool trace_cta = kTrace && static_cast<int>(blockIdx.x) == p.trace_cta;
@@ -412,9 +484,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int t = 0, li = 0, issued = 0, q_issued = -1;
         bool ok = true;
         for (int r = 0; r < rounds && ok; ++r) {
-          const int k = item_index(p, r);
+          const int k = item_at(r);
           if (k >= p.n_items) continue;
-          const Item it = decode_item(p, k);
+          const Item it = decode_at(k);
           const int qb = li & 1;
           const uint32_t qpar = static_cast<uint32_t>(li >> 1) & 1u;
           ++li;
@@ -422,10 +494,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Q(li) reuses the buffer the epilogue of item li-2 staged O in.
             ok = mbar_wait(&q_empty[qb], qpar ^ 1u, kSiteQEmpty, kDefaultWaitLimitNs, 20000u);
             if (!ok) break;
-            mbar_arrive_expect_tx(&q_full[qb], C::kTileBytes);
-            for (int h = 0; h < C::kBoxes; ++h)
-              tma_load_3d(q_buf + qb * C::kTileBytes + h * C::kBoxBytes, &q_map, &q_full[qb],
-                          h * 64, it.row0, it.zq, pol_q);
+            if constexpr (kPair) {
+              // Both CTAs' Q tiles land on the leader's barrier.
+              if (leader) mbar_arrive_expect_tx(&q_full[qb], 2 * C::kTileBytes);
+              for (int h = 0; h < C::kBoxes; ++h)
+                tma_load_3d_pair(q_buf + qb * C::kTileBytes + h * C::kBoxBytes, &q_map,
+                                 lead_bar(&q_full[qb]), h * 64, it.row0, it.zq, pol_q);
+            } else {
+              mbar_arrive_expect_tx(&q_full[qb], C::kTileBytes);
+              for (int h = 0; h < C::kBoxes; ++h)
+                tma_load_3d(q_buf + qb * C::kTileBytes + h * C::kBoxBytes, &q_map, &q_full[qb],
+                            h * 64, it.row0, it.zq, pol_q);
+            }
             q_issued = li - 1;
             tr(kEvTmaQ, qb, li - 1);
           }
@@ -436,25 +516,49 @@ __global__ void __launch_bounds__(kThreads, 1)
                              kSiteKEmpty, kDefaultWaitLimitNs, 20000u);
               if (!ok) break;
               tr(kEvTmaK, 0, t);
-              mbar_arrive_expect_tx(&k_full[ks], C::kTileBytes);
-              for (int h = 0; h < C::kBoxes; ++h)
-                tma_load_3d(k_buf + ks * C::kTileBytes + h * C::kBoxBytes, &k_map, &k_full[ks],
-                            h * 64, (it.j0 + j) * kBN, it.zkv, pol_kv);
+              if constexpr (kPair) {
+                // This CTA's 64 keys of the tile; both halves on the leader's barrier.
+                if (leader) mbar_arrive_expect_tx(&k_full[ks], 2 * C::kKTileBytes);
+                for (int h = 0; h < C::kBoxes; ++h)
+                  tma_load_3d_pair(k_buf + ks * C::kKTileBytes + h * C::kKBoxBytes, &k_map,
+                                   lead_bar(&k_full[ks]), h * 64,
+                                   (it.j0 + j) * kBN + static_cast<int>(rank) * C::kKRows,
+                                   it.zkv, pol_kv);
+              } else {
+                mbar_arrive_expect_tx(&k_full[ks], C::kTileBytes);
+                for (int h = 0; h < C::kBoxes; ++h)
+                  tma_load_3d(k_buf + ks * C::kTileBytes + h * C::kBoxBytes, &k_map, &k_full[ks],
+                              h * 64, (it.j0 + j) * kBN, it.zkv, pol_kv);
+              }
             } else {
               const int vs = t % C::kVStages;
               ok = mbar_wait(&v_empty[vs], (static_cast<uint32_t>(t / C::kVStages) & 1u) ^ 1u,
                              kSiteVEmpty, kDefaultWaitLimitNs, 20000u);
               if (!ok) break;
               tr(kEvTmaV, 0, t);
-              mbar_arrive_expect_tx(&v_full[vs], C::kTileBytes);
-              for (int h = 0; h < C::kBoxes; ++h)
-                tma_load_3d(v_buf + vs * C::kTileBytes + h * C::kBoxBytes, &v_map, &v_full[vs],
-                            h * 64, (it.j0 + j) * kBN, it.zkv, pol_kv);
+              if constexpr (kPair) {
+                // This CTA's 64 columns of d for all 128 keys.
+                if (leader) mbar_arrive_expect_tx(&v_full[vs], 2 * C::kVTileBytes);
+                for (int h = 0; h < C::kVBoxes; ++h)
+                  tma_load_3d_pair(v_buf + vs * C::kVTileBytes + h * C::kBoxBytes, &v_map,
+                                   lead_bar(&v_full[vs]),
+                                   (static_cast<int>(rank) * C::kVBoxes + h) * 64,
+                                   (it.j0 + j) * kBN, it.zkv, pol_kv);
+              } else {
+                mbar_arrive_expect_tx(&v_full[vs], C::kTileBytes);
+                for (int h = 0; h < C::kBoxes; ++h)
+                  tma_load_3d(v_buf + vs * C::kTileBytes + h * C::kBoxBytes, &v_map, &v_full[vs],
+                              h * 64, (it.j0 + j) * kBN, it.zkv, pol_kv);
+              }
             }
             issued = t + 1;
           }
         }
-        if (!ok) {
+        if (!ok && kPair && !leader) {
+          // Unwinding: this CTA's copies count on the leader's barriers; give
+          // the ones already issued time to land before the CTA exits.
+          spin_ns(200000);
+        } else if (!ok) {
           // Unwinding: let every copy already issued land before the CTA exits.
           if (is_k) {
             if (q_issued >= 0)
@@ -480,9 +584,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // only its own thread's MMAs, so each warp signals its own barriers,
       // and the S issuer learns that PV(t) has read P(t) (S buffer t % 3
       // free for S(t+3)) from p_free rather than from issue order.
-      {
+      // A pair's MMAs are all issued by its leader; the other CTA's issuer
+      // warps have nothing to do.
+      if (!kPair || leader) {
         const bool is_pv = warp == kMmaWarp;
-        Tracer<kTrace> tr(p, is_pv ? 1 : 6, trace_cta && lane == 0);
+        // The traced pair's leader records the issuers for either CTA.
+        const bool trace_issuer =
+            kPair ? (kTrace && static_cast<int>(blockIdx.x >> 1) == (p.trace_cta >> 1))
+                  : trace_cta;
+        Tracer<kTrace> tr(p, is_pv ? 1 : 6, trace_issuer && lane == 0);
         const uint32_t q_addr = smem_u32(q_buf);
         const uint32_t k_addr = smem_u32(k_buf);
         const uint32_t v_addr = smem_u32(v_buf);
@@ -493,7 +603,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t dk0 = sdesc_sw128(k_addr, 16, 1024);
         const uint64_t dv0 = sdesc_sw128(v_addr, C::kBoxBytes, 1024);
         constexpr uint32_t kTile16 = C::kTileBytes >> 4, kBox16 = C::kBoxBytes >> 4;
+        constexpr uint32_t kKTile16 = C::kKTileBytes >> 4, kKBox16 = C::kKBoxBytes >> 4;
+        constexpr uint32_t kVTile16 = C::kVTileBytes >> 4;
+        // Commits: a pair's go to the barrier in both CTAs (mask 0b11) or to
+        // the leader's only.
+        auto commit_both = [](uint64_t* b_) {
+          if constexpr (kPair)
+            mma_commit_pair_both_warp(b_, 3);
+          else
+            mma_commit_warp(b_);
+        };
+        auto commit_lead = [](uint64_t* b_) {
+          if constexpr (kPair)
+            mma_commit_pair_local_warp(b_);
+          else
+            mma_commit_warp(b_);
+        };
         const uint32_t tO = tmem_base + C::kColO;
+        // The barrier that says every epilogue reading O is done with it.
+        uint64_t* const o_rd = kPair ? o_free : o_empty;
         // Filler for unused slots of the grouped waits.
         const uint32_t dn_a = smem_u32(done), dn_p = 0;
         auto bar = [](uint64_t* b_) { return smem_u32(b_); };
@@ -513,9 +641,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           // S(t) = Q[qb] K(t)^T into S buffer t % kSBufs, once K(t) has landed
           // and PV(t - kSBufs) has consumed that buffer's P.
           for (int r = 0; r < rounds && ok; ++r) {
-            const int k = item_index(p, r);
+            const int k = item_at(r);
             if (k >= p.n_items) continue;
-            const Item it = decode_item(p, k);
+            const Item it = decode_at(k);
             const int qb = li & 1;
             const uint32_t qpar = static_cast<uint32_t>(li >> 1) & 1u;
             ++li;
@@ -528,30 +656,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                          (static_cast<uint32_t>(t / kSBufs) & 1u) ^ 1u, dn_a, dn_p, kSiteKFull);
               if (!ok) break;
               tr(kEvMmaS, qb, t);
-              const uint64_t dk = dk0 + (t % C::kKStages) * kTile16;
+              const uint64_t dk = dk0 + (t % C::kKStages) * kKTile16;
               const uint32_t ts = tmem_base + static_cast<uint32_t>(sb * 128);
 #pragma unroll
               for (int kk = 0; kk < D / 16; ++kk) {
-                const uint32_t off = (kk >> 2) * kBox16 + (kk & 3) * 2;
-                mma_ss_warp(ts, dq + off, dk + off, C::kIdescS, kk > 0 ? 1u : 0u);
+                const uint32_t off_q = (kk >> 2) * kBox16 + (kk & 3) * 2;
+                const uint32_t off_k = (kk >> 2) * kKBox16 + (kk & 3) * 2;
+                if constexpr (kPair)
+                  mma_ss_pair_warp(ts, dq + off_q, dk + off_k, C::kIdescS, kk > 0 ? 1u : 0u);
+                else
+                  mma_ss_warp(ts, dq + off_q, dk + off_k, C::kIdescS, kk > 0 ? 1u : 0u);
               }
-              mma_commit_warp(&k_empty[t % C::kKStages]);
-              mma_commit_warp(&s_ready[sb]);
+              commit_both(&k_empty[t % C::kKStages]);
+              commit_both(&s_ready[sb]);
             }
           }
         } else {
           for (int r = 0; r < rounds && ok; ++r) {
-            const int k = item_index(p, r);
+            const int k = item_at(r);
             if (k >= p.n_items) continue;
-            const Item it = decode_item(p, k);
+            const Item it = decode_at(k);
             const uint32_t oe_par = (static_cast<uint32_t>(li) & 1u) ^ 1u;  // epilogue of li-1
             if (it.n == 0) {
               // No K/V tiles: O stays unwritten (the epilogue stores zeros in Q's
               // buffer, so Q(li) must have landed first).
-              ok = wait3(bar(&q_full[li & 1]), static_cast<uint32_t>(li >> 1) & 1u, bar(o_empty),
+              ok = wait3(bar(&q_full[li & 1]), static_cast<uint32_t>(li >> 1) & 1u, bar(o_rd),
                          oe_par, dn_a, dn_p, kSiteQFull);
               if (!ok) break;
-              mma_commit_warp(o_full);
+              commit_both(o_full);
               ++li;
               continue;
             }
@@ -560,29 +692,34 @@ __global__ void __launch_bounds__(kThreads, 1)
               // V(t), P(t) and, for an item's first tile, O free (the epilogue
               // of item li-1 has read it), in one grouped wait.
               ok = wait3(bar(&v_full[t % C::kVStages]), vpar(t), bar(&p_ready[sb]),
-                         static_cast<uint32_t>(t / kSBufs) & 1u, j == 0 ? bar(o_empty) : dn_a,
+                         static_cast<uint32_t>(t / kSBufs) & 1u, j == 0 ? bar(o_rd) : dn_a,
                          j == 0 ? oe_par : dn_p, kSitePReady);
               if (!ok) break;
               tr(kEvMmaPv, 0, t);
               // O (+)= P(t) V(t): P is read from the S buffer as the A operand.
-              const uint64_t dv = dv0 + (t % C::kVStages) * kTile16;
+              const uint64_t dv = dv0 + (t % C::kVStages) * kVTile16;
               const uint32_t tp = tmem_base + static_cast<uint32_t>(sb * 128);
 #pragma unroll
-              for (int kk = 0; kk < kBN / 16; ++kk)
-                mma_ts_warp(tO, tp + kk * 8, dv + kk * (2048 >> 4), C::kIdescO,
-                            (j > 0 || kk > 0) ? 1u : 0u);
-              mma_commit_warp(&v_empty[t % C::kVStages]);
-              mma_commit_warp(&p_free[sb]);
-              mma_commit_warp(pv_done);
+              for (int kk = 0; kk < kBN / 16; ++kk) {
+                if constexpr (kPair)
+                  mma_ts_pair_warp(tO, tp + kk * 8, dv + kk * (2048 >> 4), C::kIdescO,
+                                   (j > 0 || kk > 0) ? 1u : 0u);
+                else
+                  mma_ts_warp(tO, tp + kk * 8, dv + kk * (2048 >> 4), C::kIdescO,
+                              (j > 0 || kk > 0) ? 1u : 0u);
+              }
+              commit_both(&v_empty[t % C::kVStages]);
+              commit_lead(&p_free[sb]);
+              commit_both(pv_done);
             }
             if (!ok) break;
-            mma_commit_warp(o_full);
+            commit_both(o_full);
             ++li;
           }
         }
         // Every MMA this warp issued has completed once its commit lands
         // (the barrier counts one commit from each issuer).
-        mma_commit_warp(drain);
+        commit_lead(drain);
         drain_wait(drain, 0);
         tr(kEvMmaEnd, 0, t);
       }
@@ -609,8 +746,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // K/V tiles this CTA processes in all (the global tile sequence t).
     int g_total = 0;
     for (int r = 0; r < rounds; ++r) {
-      const int k = item_index(p, r);
-      if (k < p.n_items) g_total += decode_item(p, k).n;
+      const int k = item_at(r);
+      if (k < p.n_items) g_total += decode_at(k).n;
     }
     // S(tt) lives in sr once loaded; the load of its successor in the global
     // tile sequence (also across an item boundary) is issued as soon as tile
@@ -631,9 +768,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 #pragma unroll 1
     for (int r = 0; r < rounds && ok; ++r) {
-      const int k = item_index(p, r);
+      const int k = item_at(r);
       if (k >= p.n_items) continue;
-      const Item it = decode_item(p, k);
+      const Item it = decode_at(k);
       const int qb = li & 1;
       const uint32_t tO = tmem_base + lane_addr + C::kColO;
       const int lim_a = p.causal ? min(p.Skv, it.row0 + ra + p.causal_off + 1) : p.Skv;
@@ -843,7 +980,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          mbar_arrive_warp(&p_ready[sb]);
+          if constexpr (kPair)
+            mbar_arrive_cluster_warp(lead_bar(&p_ready[sb]));  // the leader issues PV
+          else
+            mbar_arrive_warp(&p_ready[sb]);
           tr(kEvSmPublished, warp >> 2, tt);
         }
         if (have_s) {
@@ -902,9 +1042,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int li = 0;
 #pragma unroll 1
     for (int r = 0; r < rounds; ++r) {
-      const int k = item_index(p, r);
+      const int k = item_at(r);
       if (k >= p.n_items) continue;
-      const Item it = decode_item(p, k);
+      const Item it = decode_at(k);
       const int qb = li & 1;
       const uint32_t qpar = static_cast<uint32_t>(li >> 1) & 1u;
       ++li;
@@ -944,7 +1084,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      w[3]);
       };
       bool store = true;  // this unit stores the O tile
-      if (p.nsplit == 1) {
+      if (kPair || p.nsplit == 1) {
         const float inv = (have_o && ml.y > 0.0f) ? 1.0f / ml.y : 0.0f;
 #pragma unroll 1
         for (int c0 = 0; c0 < D; c0 += 32) {
@@ -962,7 +1102,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           stage16(c0 + 16, reinterpret_cast<const float*>(&o[16]));
         }
         tc_fence_before();
-        mbar_arrive(o_empty);
+        if constexpr (kPair) {
+          __syncwarp();
+          mbar_arrive_warp(o_empty);
+          mbar_arrive_cluster_warp(lead_bar(o_free));  // the leader's PV issuer reuses O
+        } else {
+          mbar_arrive(o_empty);
+        }
       } else {
         // Split unit: this unit's unnormalised O rows and (m, l) go to the
         // workspace; the Q tile's last unit to arrive merges all of them.
@@ -1074,7 +1220,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(kBarEpilogue, 128);
       if (abort_flag[0] != 0) break;
       if (quad == 0 && lane == 0) {
-        if (store) {
+        // (A pair's second tile past the last Q row has nothing to store.)
+        if (store && it.row0 < p.Sq) {
           for (int b = 0; b < C::kBoxes; ++b)
             tma_store_3d_hint(&o_map, obuf + b * C::kBoxBytes, b * 64, it.row0, it.zq, pol_o);
           bulk_commit_group();
@@ -1089,10 +1236,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---- teardown ----
   tc_fence_before();
-  __syncthreads();
+  // A pair's CTAs leave together: the leader's MMAs read the other CTA's
+  // shared memory and TMEM until its drain completes.
+  if constexpr (kPair)
+    cluster_sync_all();
+  else
+    __syncthreads();
   if (warp == kTmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (kPair)
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    else
+      tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 

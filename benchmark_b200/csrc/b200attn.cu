@@ -360,6 +360,70 @@ b200_status launch_pair(const CUtensorMap& qm, const CUtensorMap& km, const CUte
   return B200_OK;
 }
 
+// The CTA-pair d=128 kernel (cta_group::2): each cluster of two CTAs takes
+// two adjacent Q tiles of one plane and splits every K/V tile's shared-memory
+// copy between them (K: 64 keys per CTA, V: 64 columns of d per CTA).  `km`
+// is encoded with 64-row boxes.
+template <int EMU, bool TRACE>
+b200_status launch_cpair(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+                         const CUtensorMap& om, b200::attn::Params p, long long units,
+                         cudaStream_t stream) {
+  using C = b200::attn::Cfg<128, true>;
+  static unsigned attr_done = 0;
+  auto kernel = b200::attn::attention_fwd_kernel<128, EMU, TRACE, true>;
+  b200_status st = ensure_smem_attr(kernel, C::kSmemBytes, &attr_done);
+  if (st != B200_OK) return st;
+  static const int launch_regs = [kernel] {
+    cudaFuncAttributes a{};
+    return cudaFuncGetAttributes(&a, kernel) == cudaSuccess ? a.numRegs : -1;
+  }();
+  if (launch_regs != b200::attn::kLaunchRegs)
+    return fail(B200_EUNSUPPORTED,
+                "attention (CTA pairs): kernel has %d registers per thread at launch; its "
+                "register split needs exactly %d",
+                launch_regs, b200::attn::kLaunchRegs);
+  if (units > 0x3fffffffll) return fail(B200_EUNSUPPORTED, "attention: too many work units");
+  p.n_items = static_cast<int>(units);
+  p.nsplit = 1;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(b200::attn::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // Clusters of two that can be resident at once (one CTA per SM).
+  static std::mutex mu;
+  static std::map<int, int> resident;
+  int dev = 0, clusters = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = resident.find(dev);
+    if (it == resident.end()) {
+      cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        n = sm_count() / 2;
+      }
+      it = resident.emplace(dev, n).first;
+    }
+    clusters = it->second;
+  }
+  clusters = static_cast<int>(std::min<long long>(units, clusters));
+  cfg.gridDim = dim3(2 * static_cast<unsigned>(clusters), 1, 1);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, qm, km, vm, om, p);
+  if (e != cudaSuccess) return cuda_fail(e, "attention_fwd launch (CTA pairs)");
+  const cudaError_t e2 = cudaGetLastError();
+  if (e2 != cudaSuccess) return cuda_fail(e2, "attention_fwd launch (CTA pairs)");
+  return B200_OK;
+}
+
 template <int D, int EMU, bool TRACE = false>
 b200_status launch_attention(const void* q, const void* k, const void* v, void* o,
                              const AttnShape& s, cudaStream_t stream,
@@ -437,13 +501,6 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
   p.trace = tr.buf;
   p.trace_cap = tr.cap;
   p.trace_cta = tr.cta;
-  if constexpr (D == 64) {
-    // Non-causal d=64 problems that fill the GPU without a K/V split run two
-    // Q tiles per work unit (attention_pair_kernel.cuh).
-    const long long units = static_cast<long long>(pq) * ((p.n_qtiles + 1) / 2);
-    if (!s.causal && p.nsplit == 1 && units >= sm_count())
-      return launch_pair<EMU, TRACE>(qm, km, vm, om, p, units, stream);
-  }
   // Causal items are ordered in groups of planes whose K/V (shared by the
   // group's query heads under GQA) fit in about half of the 126 MB L2, so the
   // CTAs running at one time share their K/V there.  Measured on B200 at
@@ -455,6 +512,24 @@ b200_status launch_attention(const void* q, const void* k, const void* v, void* 
     const double budget = 64.0 * (1 << 20);
     const long long g = static_cast<long long>(budget / kv_bytes) * p.group;
     p.cgroup = static_cast<int>(std::max<long long>(1, std::min<long long>(g, pq)));
+  }
+  if constexpr (D == 64) {
+    // Non-causal d=64 problems that fill the GPU without a K/V split run two
+    // Q tiles per work unit (attention_pair_kernel.cuh).
+    const long long units = static_cast<long long>(pq) * ((p.n_qtiles + 1) / 2);
+    if (!s.causal && p.nsplit == 1 && units >= sm_count())
+      return launch_pair<EMU, TRACE>(qm, km, vm, om, p, units, stream);
+  } else {
+    // Non-causal d=128 problems with a pair of Q tiles for every two SMs
+    // and no K/V split run on CTA pairs (cta_group::2).
+    const long long units = static_cast<long long>(pq) * ((p.n_qtiles + 1) / 2);
+    if (!s.causal && p.nsplit == 1 && 2 * units >= sm_count()) {
+      CUtensorMap km_pair;
+      if ((st = encode_bf16_3d(&km_pair, k, D, s.Skv, pkv, 64,
+                               b200::attn::Cfg<128, true>::kKRows)) != B200_OK)
+        return st;
+      return launch_cpair<EMU, TRACE>(qm, km_pair, vm, om, p, units, stream);
+    }
   }
   // Persistent: one CTA per SM (shared memory admits one), or fewer items.
   const int grid = static_cast<int>(std::min<long long>(items, sm_count()));

@@ -98,11 +98,6 @@ constexpr uint32_t kAccEmptyArrivals = 8;  // 4 epilogue warps x 2 CTAs
 constexpr int kBarEpilogue = 1;            // named barrier of the four epilogue warps
 }  // namespace pair
 
-__device__ __forceinline__ void spin_ns(uint64_t ns) {
-  const uint64_t t0 = globaltimer_ns();
-  while (globaltimer_ns() - t0 < ns) __nanosleep(1000);
-}
-
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::kThreads, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap a_map,
                           const __grid_constant__ CUtensorMap b_map,

@@ -514,6 +514,58 @@ __device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
       : "memory");
 }
 
+__device__ __forceinline__ void mma_commit_pair_local_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// Pair MMA with A in TMEM: each CTA supplies its M/2 rows of A from its own
+// TMEM at a_tmem, and its N/2 rows of B from shared memory.
+__device__ __forceinline__ void mma_ts_pair_warp(uint32_t d_tmem, uint32_t a_tmem,
+                                                 uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// TMA 3D load into this CTA's shared memory counted on an mbarrier of either
+// CTA of the pair (`bar_cluster` from mapa_shared); no multicast.
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map,
+                                                 uint32_t bar_cluster, int x, int y, int z,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::"
+      "bytes.L2::cache_hint [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z),
+      "l"(policy)
+      : "memory");
+}
+
+// Sleep for about `ns` nanoseconds (unwinding only: lets copies this CTA
+// issued land on barriers it cannot observe).
+__device__ __forceinline__ void spin_ns(uint64_t ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < ns) __nanosleep(1000);
+}
+
+// Arrive once per warp (elected lane) on an mbarrier that may live in the
+// other CTA of the cluster, with the default (release, CTA-scope) semantics:
+// what it publishes is TMEM written by tcgen05.st and completed by
+// tcgen05.wait::st + tcgen05.fence::before_thread_sync, which the pair's MMAs
+// read; a cluster-scope release costs about 1,100 cycles per arrive here.
+__device__ __forceinline__ void mbar_arrive_cluster_warp(uint32_t cluster_addr) {
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e mbarrier.arrive.shared::cluster.b64 _, [%0];\n}\n" ::"r"(cluster_addr)
+      : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Descriptors
 // ---------------------------------------------------------------------------

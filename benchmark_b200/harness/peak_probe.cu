@@ -640,12 +640,16 @@ int main(int argc, char** argv) {
                 ops / c, ops * sms / (ms * 1e-3) / 1e9, ms);
   }
   if (probe == "softmax" || probe == "all") {
-    static const char* kNames[8] = {"ex2",          "ex2_cvt",      "cvt",
+    // The ninth line repeats pair_cvt with one warp per scheduler (128
+    // threads): what a lone softmax warp can draw from MUFU.
+    static const char* kNames[9] = {"ex2",          "ex2_cvt",      "cvt",
                                     "ex2_intpack",  "pair_cvt",     "pair_intpack",
-                                    "ex2_bf16x2",   "ex2_f16x2"};
-    for (int mode = 0; mode < 8 && rc == 0; ++mode) {
+                                    "ex2_bf16x2",   "ex2_f16x2",    "pair_cvt_1warp"};
+    for (int mode = 0; mode < 9 && rc == 0; ++mode) {
+      const int threads = mode == 8 ? 128 : 256;
       const double ms = timed([&] {
         switch (mode) {
+          case 8: softmax_mix_probe<4><<<sms, 128>>>(iters, cyc, sink); break;
           case 0: softmax_mix_probe<0><<<sms, 256>>>(iters, cyc, sink); break;
           case 1: softmax_mix_probe<1><<<sms, 256>>>(iters, cyc, sink); break;
           case 2: softmax_mix_probe<2><<<sms, 256>>>(iters, cyc, sink); break;
@@ -657,7 +661,7 @@ int main(int argc, char** argv) {
         }
       });
       const double c = mean_cycles(cyc, sms);
-      const double elems = 256.0 * 32 * iters;
+      const double elems = static_cast<double>(threads) * 32 * iters;
       std::printf("probe=softmax_%s elements_per_cycle_per_sm=%.2f value=%.1f unit=Gelem/s "
                   "ms=%.4f\n", kNames[mode], elems / c, elems * sms / (ms * 1e-3) / 1e9, ms);
     }

@@ -120,7 +120,7 @@ def test_peak_probe_all_runs_with_plausible_rates():
         "tile_issue_d128_" + m for m in ("mma_only", "commits", "commits_waits",
                                          "two_issuers_commits_waits", "two_issuers_mma_only")} | {
         "softmax_" + m for m in ("ex2", "ex2_cvt", "cvt", "ex2_intpack", "pair_cvt",
-                                 "pair_intpack", "ex2_bf16x2", "ex2_f16x2")}
+                                 "pair_intpack", "ex2_bf16x2", "ex2_f16x2", "pair_cvt_1warp")}
     assert vals["mma_m128_n256_ss_1acc"] > 500  # TFLOP/s
     assert vals["hbm_copy_1GiB"] > 1000        # GB/s
     assert all(v > 0 for v in vals.values())
