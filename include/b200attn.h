@@ -61,6 +61,8 @@ typedef enum {
  * Replaces the launch of qk_tma_mma_ld_kernel in 0.attention/main.cu:521-569
  * (benchmark) and 0.attention/main.cu:1901-1911 (fused validation); accepts
  * every shape the scalar path accepts (0.attention/main.cu:1706-1721) plus D=64.
+ * Non-causal D=128 problems with a pair of Q tiles per two SMs run on
+ * clusters of two CTAs (tcgen05 cta_group::2); the results are the same bits.
  */
 b200_status attention_fwd(const void* q, const void* k, const void* v, void* o, int B, int Hq,
                           int Hkv, int Sq, int Skv, int D, int causal, float softmax_scale,
@@ -102,7 +104,9 @@ b200_status attention_fwd_noalloc(const void* q, const void* k, const void* v, v
  * {(event << 32) | (tile << 24) | iteration, clock64()}; the iteration of
  * TMA, MMA and softmax records is the CTA's global K/V tile index (for
  * non-causal d=64 problems, traced on the two-Q-tile kernel that runs them:
- * the S index, with the pipe as the tile field).  Events
+ * the S index, with the pipe as the tile field; for problems that run on CTA
+ * pairs the MMA issuers of the traced CTA's pair are recorded, which live in
+ * its even CTA).  Events
  * are listed in benchmark_b200/trace.py, which also writes the reference's
  * per-iteration trace CSV.  Stands in for the reference's
  * ATTENTION_CLOCK_TRACE build and its per-stage CSV
