@@ -73,7 +73,7 @@ WORKLOADS = {
 # the full problem by its items (the traffic grows with them: each batch
 # streams its own K/V once); c3 was captured on the full 64-head problem.
 NCU_TRAFFIC_BYTES = {
-    "c2": 514.55e6,     # profiles/attention_fwd_d128_c2_b4h32n4096.md
+    "c2": 517.23e6,     # profiles/attention_fwd_d128_c2_b4h32n4096.md
     "c1": 6.37e6,       # profiles/attention_fwd_d128_c1_b1h8n1024.md
     "c3": 3.06e9,       # profiles/attention_fwd_d128_c3_causal_h64n16384_l2.md
     "c4": 8 * 107.00e6,  # profiles/attention_fwd_d64_c4_b8h16n2048.md
