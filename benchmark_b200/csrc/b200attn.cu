@@ -360,6 +360,50 @@ b200_status launch_pair(const CUtensorMap& qm, const CUtensorMap& km, const CUte
   return B200_OK;
 }
 
+// Launch `kernel` on clusters of two CTAs (one per SM): as many clusters as
+// can be resident at once (cached per device and kernel), or `units`.
+template <typename Kernel, typename... Args>
+b200_status launch_cluster2(Kernel kernel, int smem_bytes, long long units, cudaStream_t stream,
+                            const char* what, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(b200::attn::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> resident;
+  int dev = 0, clusters = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kernel));
+    auto it = resident.find(key);
+    if (it == resident.end()) {
+      cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        n = sm_count() / 2;
+      }
+      it = resident.emplace(key, n).first;
+    }
+    clusters = it->second;
+  }
+  clusters = static_cast<int>(std::min<long long>(units, clusters));
+  cfg.gridDim = dim3(2 * static_cast<unsigned>(clusters), 1, 1);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  const cudaError_t e2 = cudaGetLastError();
+  if (e2 != cudaSuccess) return cuda_fail(e2, what);
+  return B200_OK;
+}
+
 // The CTA-pair d=128 kernel (cta_group::2): each cluster of two CTAs takes
 // two adjacent Q tiles of one plane and splits every K/V tile's shared-memory
 // copy between them (K: 64 keys per CTA, V: 64 columns of d per CTA).  `km`
@@ -385,43 +429,8 @@ b200_status launch_cpair(const CUtensorMap& qm, const CUtensorMap& km, const CUt
   if (units > 0x3fffffffll) return fail(B200_EUNSUPPORTED, "attention: too many work units");
   p.n_items = static_cast<int>(units);
   p.nsplit = 1;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cudaLaunchConfig_t cfg{};
-  cfg.blockDim = dim3(b200::attn::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = C::kSmemBytes;
-  cfg.stream = stream;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  // Clusters of two that can be resident at once (one CTA per SM).
-  static std::mutex mu;
-  static std::map<int, int> resident;
-  int dev = 0, clusters = 0;
-  cudaGetDevice(&dev);
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    auto it = resident.find(dev);
-    if (it == resident.end()) {
-      cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n < 1) {
-        cudaGetLastError();
-        n = sm_count() / 2;
-      }
-      it = resident.emplace(dev, n).first;
-    }
-    clusters = it->second;
-  }
-  clusters = static_cast<int>(std::min<long long>(units, clusters));
-  cfg.gridDim = dim3(2 * static_cast<unsigned>(clusters), 1, 1);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, qm, km, vm, om, p);
-  if (e != cudaSuccess) return cuda_fail(e, "attention_fwd launch (CTA pairs)");
-  const cudaError_t e2 = cudaGetLastError();
-  if (e2 != cudaSuccess) return cuda_fail(e2, "attention_fwd launch (CTA pairs)");
-  return B200_OK;
+  return launch_cluster2(kernel, C::kSmemBytes, units, stream, "attention_fwd launch (CTA pairs)",
+                         qm, km, vm, om, p);
 }
 
 template <int D, int EMU, bool TRACE = false>
