@@ -1,8 +1,9 @@
 """GPU checks of attention_fwd_trace (the clock-trace build): the traced
 kernels compute the same bytes as attention_fwd, every role records, and the
 decoder's stage summary and reference-format rows come out of a real trace,
-for the one-Q-tile kernel (d=128) and the two-Q-tile kernel (non-causal
-d=64)."""
+for the one-Q-tile kernel on CTA pairs (non-causal d=128, 128 Q-tile pairs)
+and on one CTA per Q tile (causal d=128), and the two-Q-tile kernel
+(non-causal d=64)."""
 import pytest
 import torch
 
@@ -13,8 +14,8 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("B,H,N,D,causal", [
-    (2, 8, 2048, 128, False),   # one-Q-tile kernel
-    (1, 4, 2048, 128, True),    # one-Q-tile kernel, causal
+    (2, 8, 2048, 128, False),   # one-Q-tile kernel on CTA pairs (CTA 3's pair leader issues)
+    (1, 4, 2048, 128, True),    # one-Q-tile kernel, causal, one CTA per Q tile
     (8, 16, 2048, 64, False),   # two-Q-tile kernel (1024 units)
 ])
 def test_trace_matches_and_records(B, H, N, D, causal):
