@@ -77,8 +77,8 @@ NCU_TRAFFIC_BYTES = {
     "c1": 6.37e6,       # profiles/attention_fwd_d128_c1_b1h8n1024.md
     "c3": 3.06e9,       # profiles/attention_fwd_d128_c3_causal_h64n16384_l2.md
     "c4": 8 * 107.00e6,  # profiles/attention_fwd_d64_c4_b8h16n2048.md
-    "gemm": 1148.0e6,   # profiles/gemm_bf16_pair_8192_b_row_major.md
-    "gemm16k": 18.04e9,  # profiles/gemm_bf16_pair_16384_b_row_major.md
+    "gemm": 1044.0e6,   # profiles/gemm_bf16_pair_8192_b_row_major.md (current build)
+    "gemm16k": 16.35e9,  # profiles/gemm_bf16_pair_16384_b_row_major.md (current build)
 }
 
 L2_BYTES = 126 * 2**20
